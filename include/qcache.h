@@ -1,0 +1,208 @@
+/*
+ * qcache.h — C ABI of the B200 (sm_100a) per-token cache path of the
+ * Qwen3.5-9B hybrid stack (24 Gated-DeltaNet layers + 8 full-attention
+ * layers).
+ *
+ * In the reference engine this path is inline host C++ inside
+ * forward_decode()/forward_prefill() and generate() (src/engine.cpp), with
+ * file-scope globals for the caches.  This header is the thin boundary that
+ * replaces those blocks: the engine keeps its public API (src/engine.h:69-90)
+ * and calls these functions where it used to run the host math.
+ *
+ * Conventions (mirroring the reference's, src/engine.cpp:79-97, 4164-4176):
+ *   - every call returns an int status (QC_OK == 0); nothing throws, nothing
+ *     exits; qc_last_error() returns a message for the last failure;
+ *   - one context per GPU, externally synchronised (the reference serialises
+ *     inference behind one mutex, src/server.cpp:20,125);
+ *   - tensors named *_dev are device pointers owned by the caller; all device
+ *     work is enqueued on the caller's stream (a cudaStream_t passed as void*);
+ *   - the context owns the KV page pool, the DeltaNet state, the conv rings,
+ *     the prefix snapshots and the page tables;
+ *   - bf16 values travel as uint16_t bit patterns; f32 -> bf16 conversions done
+ *     by this library round to nearest even.
+ */
+#ifndef QCACHE_H
+#define QCACHE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- fixed model shapes (src/model_config.h:15-33, src/engine.cpp:2383-2393) ---- */
+#define QC_N_HEAD        16
+#define QC_N_HEAD_KV     4
+#define QC_HEAD_DIM      256
+#define QC_ROPE_DIM      64
+#define QC_ATTN_Q_DIM    (QC_N_HEAD * QC_HEAD_DIM * 2)         /* 8192: [16][q 256 | gate 256] */
+#define QC_ATTN_PROJ     (QC_ATTN_Q_DIM + 2 * QC_N_HEAD_KV * QC_HEAD_DIM) /* 10240 */
+#define QC_ATTN_OUT      (QC_N_HEAD * QC_HEAD_DIM)             /* 4096 */
+#define QC_GDN_K_HEADS   16
+#define QC_GDN_V_HEADS   32
+#define QC_GDN_HEAD      128
+#define QC_CONV_CH       8192                                  /* q 2048 | k 2048 | v 4096 */
+#define QC_CONV_TAPS     4
+#define QC_GDN_PROJ      12352                                 /* conv 8192 | z 4096 | alpha 32 | beta 32 */
+#define QC_GDN_OUT       4096
+#define QC_GDN_STATE     (QC_GDN_V_HEADS * QC_GDN_HEAD * QC_GDN_HEAD) /* floats per layer per sequence */
+#define QC_PAGE          64                                    /* tokens per KV page */
+
+/* ---- status codes ---- */
+#define QC_OK            0
+#define QC_ERR_ARG       1   /* bad argument / state (message in qc_last_error) */
+#define QC_ERR_OOM       2   /* page pool, sequence slots or snapshot slots exhausted */
+#define QC_ERR_CUDA      3   /* a CUDA runtime call failed */
+#define QC_ERR_TIMEOUT   4   /* a bounded device wait expired (kernel returned early) */
+#define QC_ERR_BOUNDS    5   /* a device-side index check failed (access skipped) */
+#define QC_ERR_NODEVICE  6   /* device work requested on a host-only context */
+
+/* qc_create(device = QC_DEVICE_NONE) makes a host-only context: page
+ * allocation, sequence bookkeeping and the prefix table work, every call that
+ * would touch the GPU returns QC_ERR_NODEVICE.  It exists to test the host
+ * logic on machines without a GPU; it computes nothing. */
+#define QC_DEVICE_NONE   (-1)
+
+typedef struct qc_ctx qc_ctx;
+typedef void* qc_stream;   /* cudaStream_t */
+
+typedef struct qc_config {
+  int32_t n_attn_layers;   /* full-attention layers (8) */
+  int32_t n_gdn_layers;    /* Gated-DeltaNet layers (24) */
+  int32_t max_seqs;        /* live sequence slots */
+  int32_t max_pages;       /* physical KV pages (QC_PAGE tokens each, all attention layers) */
+  int32_t max_ctx;         /* positions per sequence; size of the RoPE table */
+  int32_t max_batch;       /* sequences per decode step */
+  int32_t max_snapshots;   /* DeltaNet/conv snapshot slots of the prefix cache */
+  int32_t flags;           /* reserved, 0 */
+} qc_config;
+
+/* ---------------------------------------------------------------- context */
+
+/* Replaces the cache allocations of load_model_and_tokenizer
+ * (src/engine.cpp:3835-3843) and precompute_rope (src/engine.cpp:2408-2420,
+ * called at src/engine.cpp:3850-3853). */
+int qc_create(const qc_config* cfg, int device, qc_ctx** out);
+void qc_destroy(qc_ctx* ctx);
+const char* qc_last_error(const qc_ctx* ctx);
+/* Reads and clears the device error word written by kernels (QC_ERR_TIMEOUT /
+ * QC_ERR_BOUNDS); synchronises the given stream first. */
+int qc_check_device(qc_ctx* ctx, qc_stream stream);
+
+/* Per-layer small weights, host pointers, copied to the device.
+ * Attention: q_norm, k_norm [256] (cache_small_weights, src/engine.cpp:1819-1821).
+ * DeltaNet: ssm_a [32] (already negative, = -exp(A_log)), dt_bias [32],
+ * ssm_norm [128], conv_w [4][8192] tap-major (the transposed layout built by
+ * src/gguf_loader.cpp:389-396). */
+int qc_set_attn_params(qc_ctx* ctx, int attn_layer, const float* q_norm, const float* k_norm);
+int qc_set_gdn_params(qc_ctx* ctx, int gdn_layer, const float* ssm_a, const float* dt_bias,
+                      const float* ssm_norm, const float* conv_w);
+
+/* -------------------------------------------------------------- sequences */
+
+int qc_seq_alloc(qc_ctx* ctx, int32_t* seq);
+int qc_seq_free(qc_ctx* ctx, int32_t seq);
+/* reset_state() for one sequence (src/engine.cpp:4164-4176): zero the DeltaNet
+ * state and conv ring, release the KV pages, forget the cached tokens. */
+int qc_seq_reset(qc_ctx* ctx, int32_t seq, qc_stream stream);
+int qc_seq_len(const qc_ctx* ctx, int32_t seq, int32_t* len);
+/* Number of KV pages mapped by the sequence and their physical ids. */
+int qc_seq_pages(const qc_ctx* ctx, int32_t seq, int32_t* pages, int32_t cap, int32_t* n_pages);
+
+/* Back positions [0, new_len) with pages and set the length (no data written).
+ * Used to stand up an existing context before writing it with qc_kv_write. */
+int qc_seq_reserve(qc_ctx* ctx, int32_t seq, int32_t new_len);
+/* Scatter n positions starting at pos0 from a contiguous [n][4][256] bf16
+ * device array into the sequence's pages of one attention layer (and the
+ * gather that reads them back).  Bit copies. */
+int qc_kv_write(qc_ctx* ctx, int32_t seq, int attn_layer, int32_t pos0, int32_t n,
+                const uint16_t* k_dev, const uint16_t* v_dev, qc_stream stream);
+int qc_kv_read(qc_ctx* ctx, int32_t seq, int attn_layer, int32_t pos0, int32_t n,
+               uint16_t* k_dev, uint16_t* v_dev, qc_stream stream);
+/* DeltaNet recurrent state [32][128][128] f32 and conv history [3][8192] bf16
+ * (oldest token first, the layout of g_conv_state, src/engine.cpp:92-94,
+ * 3215-3233) of one layer of one sequence, device pointers. */
+int qc_gdn_state_write(qc_ctx* ctx, int32_t seq, int gdn_layer, const float* state_dev,
+                       const uint16_t* conv_dev, qc_stream stream);
+int qc_gdn_state_read(qc_ctx* ctx, int32_t seq, int gdn_layer, float* state_dev,
+                      uint16_t* conv_dev, qc_stream stream);
+
+/* ----------------------------------------------------------- decode step */
+
+/* Start one decode token for n sequences (n <= max_batch): each sequence's
+ * token goes to position len(seq) (g_pos in the reference); a page is mapped
+ * when the position opens one.  tokens (host, may be NULL) are recorded in the
+ * sequences' token history (g_cached_tokens.push_back, src/engine.cpp:4151). */
+int qc_decode_begin(qc_ctx* ctx, const int32_t* seq_ids, int32_t n, const int32_t* tokens,
+                    qc_stream stream);
+/* Full-attention layer for the batch (src/engine.cpp:3485-3564):
+ * proj_dev [n][10240] bf16 -> out_dev [n][4096] bf16.  Fused per-head Q/K
+ * RMSNorm, partial RoPE, bf16 KV append, split-K GQA flash-decode, sigmoid
+ * output gate. */
+int qc_attn_decode(qc_ctx* ctx, int attn_layer, const uint16_t* proj_dev, uint16_t* out_dev,
+                   qc_stream stream);
+/* Gated-DeltaNet layer for the batch (src/engine.cpp:3204-3327):
+ * proj_dev [n][12352] bf16 -> out_dev [n][4096] bf16.  Causal conv ring +
+ * SiLU, L2-normalised q/k, decay/beta, delta-rule state update, gated RMSNorm. */
+int qc_gdn_decode(qc_ctx* ctx, int gdn_layer, const uint16_t* proj_dev, uint16_t* out_dev,
+                  qc_stream stream);
+/* Commit the token: len(seq) += 1 for every sequence of the batch (g_pos++,
+ * src/engine.cpp:4150). */
+int qc_decode_end(qc_ctx* ctx);
+
+/* ----------------------------------------------------------- prefix cache */
+
+/* The reference's single-sequence prefix rule (src/engine.cpp:4058-4080):
+ * longest common prefix of tokens against the sequence's recorded history;
+ * if the history diverges, or the whole prompt is already cached, the
+ * sequence is reset and *prefix_len = 0.  Afterwards the caller prefills
+ * tokens[*prefix_len:]. */
+int qc_seq_match_prefix(qc_ctx* ctx, int32_t seq, const int32_t* tokens, int32_t n,
+                        int32_t* prefix_len, qc_stream stream);
+
+/* Hashed prefix cache (no reference counterpart: the reference keeps one
+ * token vector, src/engine.cpp:96-97).  An entry holds a token prefix of
+ * length P, the KV pages that cover it (full pages shared by refcount, the
+ * partial tail page copied) and a DeltaNet/conv snapshot taken at P.
+ *
+ * insert: snapshot sequence `seq` (its length must equal n and its history
+ *         must equal tokens) as a new entry.
+ * lookup: longest entry whose tokens are a prefix of tokens[0:n] with P < n
+ *         (at least one token is left to prefill, as in the reference);
+ *         *entry = -1 and *matched = 0 on a miss.  Host only.
+ * restore: for i < n, give seqs[i] (freshly reset) the state of entries[i]:
+ *         page-table gather, tail-page copy-on-write, snapshot restore; one
+ *         batched launch.  Afterwards len(seqs[i]) = P(entries[i]).
+ * release: drop an entry (pages are freed when no sequence maps them). */
+int qc_prefix_insert(qc_ctx* ctx, int32_t seq, const int32_t* tokens, int32_t n, int32_t* entry,
+                     qc_stream stream);
+int qc_prefix_lookup(qc_ctx* ctx, const int32_t* tokens, int32_t n, int32_t* matched,
+                     int32_t* entry);
+int qc_prefix_restore(qc_ctx* ctx, const int32_t* entries, const int32_t* seqs, int32_t n,
+                      qc_stream stream);
+int qc_prefix_release(qc_ctx* ctx, int32_t entry);
+/* Bytes the last qc_prefix_restore call moved on the device (read + write). */
+int qc_prefix_last_restore_bytes(const qc_ctx* ctx, int64_t* bytes);
+/* Chained page hash h_i = H(h_{i-1}, tokens[64i:64i+64]) for the n/64 full
+ * pages of tokens (pure host function). */
+int qc_prefix_page_hashes(const int32_t* tokens, int32_t n, uint64_t* hashes);
+
+/* --------------------------------------------- split-K across GPUs (long ctx) */
+
+/* Partial attention of the current decode batch's sequence 0 over the KV
+ * pages [page_begin, page_end) that this context maps (positions outside the
+ * range are not read).  Writes per q-head m (running max, log2 domain),
+ * l (sum) and o[256] (unnormalised) as partial_dev [16][2 + 256] f32.  The
+ * context that owns the page of the new position appends the token (append
+ * != 0).  qc_attn_combine merges G such partials and applies the gate. */
+int qc_attn_partial(qc_ctx* ctx, int attn_layer, const uint16_t* proj_dev, int32_t page_begin,
+                    int32_t page_end, int32_t append, float* partial_dev, qc_stream stream);
+int qc_attn_combine(qc_ctx* ctx, const float* partials_dev, int32_t n_parts,
+                    const uint16_t* proj_dev, uint16_t* out_dev, qc_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QCACHE_H */

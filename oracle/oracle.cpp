@@ -1,0 +1,435 @@
+// oracle.cpp — CPU restatement of the reference's per-token cache-path math.
+//
+// TEST INFRASTRUCTURE ONLY.  Only tests/, __graft_entry__.smoke() and the
+// cpu_baseline / --impl reference legs of bench.py may load this library; the
+// product (libqcache.so) never links or calls it.
+//
+// Parity status: UNPINNED by the reference's own tests.  The reference
+// (vibekernels/qwen3.5-9b-bfp8b-1xn300) ships no unit test, golden vector or
+// fixture for this path (its only cache test, src/tests/test_inference.cpp:
+// 209-254, asserts n_tokens > 0), and its engine cannot be compiled here
+// (src/engine.cpp:13-21 needs tt-metalium).  This file restates the cited
+// lines; tests/test_oracle.py cross-checks it against an independent float64
+// numpy restatement and known-answer cases, and tests/golden/ freezes its
+// outputs.
+//
+// Math modes:
+//   QO_EXACT      libm expf/logf/sqrtf everywhere.  The GPU kernels are judged
+//                 against this mode.
+//   QO_REF_APPROX Schraudolph exp in softplus, the beta / attention-gate
+//                 sigmoids and every SiLU, as the reference does
+//                 (src/engine.cpp:2349-2376); reported only to show how far the
+//                 reference itself sits from exact math.
+//
+// Storage follows the build, not the reference, where the build changes it:
+// KV is bf16 (the reference keeps fp32, src/engine.cpp:81-84), appended with
+// round-to-nearest-even.  The appended K is computed with the operation order
+// of qo_k_append below, which the CUDA kernel follows operation by operation,
+// so the appended bytes are identical.
+//
+// Compiled twice from this one source (oracle/Makefile): liboracle.so with
+// -O2 -ffp-contract=off (parity) and liboracle_fast.so with the reference's
+// -O3 -ffast-math (the timed CPU baseline, src Makefile:47,66).
+
+#include <algorithm>
+#include <atomic>
+#include <cfloat>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+namespace {
+
+constexpr int N_HEAD = 16, N_KV = 4, HD = 256, ROPE = 64, HALF = ROPE / 2;
+constexpr int Q_DIM = N_HEAD * HD * 2;            // 8192, q|gate interleaved per head
+constexpr int KV_DIM = N_KV * HD;                 // 1024
+constexpr int ATTN_PROJ = Q_DIM + 2 * KV_DIM;     // 10240
+constexpr int KH = 16, VH = 32, HK = 128, HV = 128;
+constexpr int CONV_CH = 8192, GDN_PROJ = 12352;
+constexpr float EPS = 1e-6f;
+constexpr float ATTN_SCALE = 1.0f / 16.0f;        // src/model_config.h:40
+constexpr float SSM_SCALE = 1.0f / 11.3137f;      // src/engine.cpp:3249
+
+enum { QO_EXACT = 0, QO_REF_APPROX = 1 };
+
+inline float bf16_to_f32(uint16_t b) {
+  uint32_t u = uint32_t(b) << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+// Round to nearest even (the build's convention; NaN kept quiet).
+inline uint16_t f32_to_bf16_rne(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return uint16_t((u >> 16) | 0x40);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return uint16_t(u >> 16);
+}
+// The reference's conversion: truncation (src/engine.cpp:248-252).
+inline uint16_t f32_to_bf16_trunc(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  return uint16_t(u >> 16);
+}
+
+// Schraudolph exp, restated from src/engine.cpp:2349-2356.
+inline float fast_expf(float x) {
+  x = std::max(-88.0f, std::min(88.0f, x));
+  int32_t i = int32_t(12102203.0f * x + 1065353216.0f);
+  float f;
+  std::memcpy(&f, &i, 4);
+  return f;
+}
+inline float mexp(float x, int mode) { return mode == QO_REF_APPROX ? fast_expf(x) : std::exp(x); }
+inline float msigmoid(float x, int mode) { return 1.0f / (1.0f + mexp(-x, mode)); }
+inline float msilu(float x, int mode) { return x * msigmoid(x, mode); }
+
+// RoPE table entry, restated from precompute_rope (src/engine.cpp:2408-2420).
+inline void rope_entry(int pos, int p, float* c, float* s) {
+  float freq = 1.0f / powf(10000000.0f, 2.0f * p / ROPE);
+  float theta = pos * freq;
+  *c = cosf(theta);
+  *s = sinf(theta);
+}
+
+// Per-head RMSNorm + partial RoPE of one 256-wide head, in the operation order
+// the CUDA kernel uses (lane l of a warp owns dims 8l..8l+7):
+//   ss_l = fma-chain of x^2 over the lane's 8 dims, then an xor butterfly
+//   (16, 8, 4, 2, 1) of additions; rms = 1 / sqrt(ss / 256 + eps);
+//   y = (x * rms) * w; RoPE on dims [0, 64) pairs (p, p + 32) with every
+//   product rounded before the add.
+// Math of src/engine.cpp:3497-3519 (RMSNorm) and 2422-2432 (apply_rope_cached).
+void qk_norm_rope(const float* x, const float* w, const float* cs, const float* sn, float* y) {
+  float lane[32];
+  for (int l = 0; l < 32; ++l) {
+    float s = 0.0f;
+    for (int j = 0; j < 8; ++j) s = std::fma(x[8 * l + j], x[8 * l + j], s);
+    lane[l] = s;
+  }
+  for (int m = 16; m >= 1; m >>= 1) {
+    float t[32];
+    for (int l = 0; l < 32; ++l) t[l] = lane[l] + lane[l ^ m];
+    std::memcpy(lane, t, sizeof(t));
+  }
+  volatile float ss = lane[0];
+  volatile float var = ss / 256.0f + EPS;
+  volatile float root = std::sqrt((float)var);
+  float rms = 1.0f / root;
+  for (int d = 0; d < HD; ++d) {
+    volatile float a = x[d] * rms;
+    y[d] = a * w[d];
+  }
+  for (int p = 0; p < HALF; ++p) {
+    float y0 = y[p], y1 = y[p + HALF];
+    volatile float a = y0 * cs[p], b = y1 * sn[p], c = y1 * cs[p], d = y0 * sn[p];
+    y[p] = a - b;
+    y[p + HALF] = c + d;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+// ---------------------------------------------------------------- helpers
+
+void qo_bf16_round(const float* x, uint16_t* y, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) y[i] = f32_to_bf16_rne(x[i]);
+}
+void qo_bf16_trunc(const float* x, uint16_t* y, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) y[i] = f32_to_bf16_trunc(x[i]);
+}
+void qo_bf16_widen(const uint16_t* x, float* y, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) y[i] = bf16_to_f32(x[i]);
+}
+float qo_fast_expf(float x) { return fast_expf(x); }
+void qo_rope_table(int pos, float* cs, float* sn) {
+  for (int p = 0; p < HALF; ++p) rope_entry(pos, p, &cs[p], &sn[p]);
+}
+
+// K append of one token: k_proj [4][256] bf16 -> k_out [4][256] bf16
+// (RMSNorm with k_norm, RoPE at pos, RNE).  V is appended unchanged.
+void qo_k_append(const uint16_t* k_proj, const float* k_norm, int pos, uint16_t* k_out) {
+  float cs[HALF], sn[HALF];
+  qo_rope_table(pos, cs, sn);
+  for (int h = 0; h < N_KV; ++h) {
+    float x[HD], y[HD];
+    for (int d = 0; d < HD; ++d) x[d] = bf16_to_f32(k_proj[h * HD + d]);
+    qk_norm_rope(x, k_norm, cs, sn, y);
+    for (int d = 0; d < HD; ++d) k_out[h * HD + d] = f32_to_bf16_rne(y[d]);
+  }
+}
+
+// ------------------------------------------------------------- attention
+
+// One full-attention decode step for one sequence (src/engine.cpp:3485-3564).
+//   proj  [10240] bf16: [16][q 256 | gate 256], k [4][256], v [4][256]
+//   k_cache, v_cache [pos + 1][4][256] bf16; rows [0, pos) hold the existing
+//         context, row pos is written here (the append, src/engine.cpp:3521-3526)
+//   out   [16][256] f32 (before the bf16 hand-off)
+// Online softmax over positions with exact expf (src/engine.cpp:3538-3559),
+// out = acc / sum * sigmoid(gate) (src/engine.cpp:3560-3563).
+void qo_attn_decode(const uint16_t* proj, const float* q_norm, const float* k_norm, int pos,
+                    uint16_t* k_cache, uint16_t* v_cache, float* out, int mode) {
+  float cs[HALF], sn[HALF];
+  qo_rope_table(pos, cs, sn);
+  qo_k_append(proj + Q_DIM, k_norm, pos, k_cache + (int64_t)pos * KV_DIM);
+  std::memcpy(v_cache + (int64_t)pos * KV_DIM, proj + Q_DIM + KV_DIM, KV_DIM * sizeof(uint16_t));
+  const int kv_len = pos + 1;
+  std::vector<float> kf((int64_t)kv_len * HD), vf((int64_t)kv_len * HD);
+  for (int h = 0; h < N_HEAD; ++h) {
+    const int kvh = h / (N_HEAD / N_KV);
+    if (h % (N_HEAD / N_KV) == 0) {
+      for (int p = 0; p < kv_len; ++p)
+        for (int d = 0; d < HD; ++d) {
+          kf[(int64_t)p * HD + d] = bf16_to_f32(k_cache[(int64_t)p * KV_DIM + kvh * HD + d]);
+          vf[(int64_t)p * HD + d] = bf16_to_f32(v_cache[(int64_t)p * KV_DIM + kvh * HD + d]);
+        }
+    }
+    float x[HD], q[HD];
+    for (int d = 0; d < HD; ++d) x[d] = bf16_to_f32(proj[h * 2 * HD + d]);
+    qk_norm_rope(x, q_norm, cs, sn, q);
+    float acc[HD] = {0};
+    float mx = -FLT_MAX, sum = 0.0f;
+    for (int p = 0; p < kv_len; ++p) {
+      const float* kr = &kf[(int64_t)p * HD];
+      float dot = 0.0f;
+      for (int d = 0; d < HD; ++d) dot += q[d] * kr[d];
+      float score = dot * ATTN_SCALE;
+      float nm = std::max(mx, score);
+      float e = std::exp(score - nm);
+      float corr = std::exp(mx - nm);
+      sum = sum * corr + e;
+      const float* vr = &vf[(int64_t)p * HD];
+      for (int d = 0; d < HD; ++d) acc[d] = acc[d] * corr + e * vr[d];
+      mx = nm;
+    }
+    for (int d = 0; d < HD; ++d) {
+      float g = bf16_to_f32(proj[h * 2 * HD + HD + d]);
+      out[h * HD + d] = (acc[d] / sum) * msigmoid(g, mode);
+    }
+  }
+}
+
+// Partial attention over positions [p_begin, p_end) of an already-appended
+// cache, for the long-context split over devices.  Writes, per q-head,
+// m (max of score * log2(e)), l (sum of 2^(s - m)) and o[256] (unnormalised),
+// as partial [16][258].  Used by the multi-rank tests as the rank-local math.
+void qo_attn_partial(const uint16_t* proj, const float* q_norm, int pos, const uint16_t* k_cache,
+                     const uint16_t* v_cache, int p_begin, int p_end, float* partial) {
+  const float LOG2E = 1.4426950408889634f;
+  float cs[HALF], sn[HALF];
+  qo_rope_table(pos, cs, sn);
+  for (int h = 0; h < N_HEAD; ++h) {
+    const int kvh = h / (N_HEAD / N_KV);
+    float x[HD], q[HD];
+    for (int d = 0; d < HD; ++d) x[d] = bf16_to_f32(proj[h * 2 * HD + d]);
+    qk_norm_rope(x, q_norm, cs, sn, q);
+    float* rec = partial + h * (HD + 2);
+    double m = -INFINITY, l = 0.0;
+    std::vector<double> acc(HD, 0.0);
+    for (int p = p_begin; p < p_end; ++p) {
+      double dot = 0.0;
+      for (int d = 0; d < HD; ++d)
+        dot += (double)q[d] * bf16_to_f32(k_cache[(int64_t)p * KV_DIM + kvh * HD + d]);
+      double s = dot * ATTN_SCALE * LOG2E;
+      double nm = std::max(m, s);
+      double corr = std::exp2(m - nm), e = std::exp2(s - nm);
+      l = l * corr + e;
+      for (int d = 0; d < HD; ++d)
+        acc[d] = acc[d] * corr + e * bf16_to_f32(v_cache[(int64_t)p * KV_DIM + kvh * HD + d]);
+      m = nm;
+    }
+    rec[0] = (float)m;
+    rec[1] = (float)l;
+    for (int d = 0; d < HD; ++d) rec[2 + d] = (float)acc[d];
+  }
+}
+
+// Merge G partials [G][16][258] and apply the sigmoid gate -> out [16][256] f32.
+void qo_attn_combine(const float* partials, int n_parts, const uint16_t* proj, float* out) {
+  for (int h = 0; h < N_HEAD; ++h) {
+    double M = -INFINITY;
+    for (int g = 0; g < n_parts; ++g) M = std::max(M, (double)partials[(g * N_HEAD + h) * (HD + 2)]);
+    double L = 0.0;
+    std::vector<double> acc(HD, 0.0);
+    for (int g = 0; g < n_parts; ++g) {
+      const float* rec = partials + (g * N_HEAD + h) * (HD + 2);
+      if (rec[1] == 0.0f) continue;
+      double w = std::exp2((double)rec[0] - M);
+      L += w * rec[1];
+      for (int d = 0; d < HD; ++d) acc[d] += w * rec[2 + d];
+    }
+    for (int d = 0; d < HD; ++d) {
+      float g = bf16_to_f32(proj[h * 2 * HD + HD + d]);
+      out[h * HD + d] = (float)(acc[d] / L) * (1.0f / (1.0f + std::exp(-g)));
+    }
+  }
+}
+
+// --------------------------------------------------------- Gated DeltaNet
+
+// One Gated-DeltaNet decode step for one sequence, v-heads [vh0, vh1).
+//   proj  [12352] bf16: conv input [8192] | z [4096] | alpha [32] | beta [32]
+//   state [32][128][128] f32, row i (v-dim) over j (k-dim) contiguous
+//         (src/engine.cpp:3282-3286), updated in place
+//   conv  [3][8192] f32 history, oldest first, updated in place (shift)
+//   conv_w [4][8192] tap-major (src/gguf_loader.cpp:389-396)
+//   out   [4096] f32
+// Restates src/engine.cpp:3204-3324.
+static void gdn_heads(const uint16_t* proj, float* state, const float* ssm_a,
+                      const float* dt_bias, const float* ssm_norm, float* out, int mode, int vh0,
+                      int vh1, const float* conv_out) {
+  float zf[HV];
+  for (int vh = vh0; vh < vh1; ++vh) {
+    const int kh = vh % KH;  // src/engine.cpp:3254
+    float q[HK], k[HK], v[HV];
+    for (int d = 0; d < HK; ++d) {
+      q[d] = conv_out[kh * HK + d];
+      k[d] = conv_out[KH * HK + kh * HK + d];
+    }
+    for (int d = 0; d < HV; ++d) v[d] = conv_out[2 * KH * HK + vh * HV + d];
+    // L2 normalisation: 1 / sqrt(sum x^2 + eps) (src/engine.cpp:3261-3275)
+    float qn = 0.0f, kn = 0.0f;
+    for (int d = 0; d < HK; ++d) {
+      qn += q[d] * q[d];
+      kn += k[d] * k[d];
+    }
+    const float qs = 1.0f / std::sqrt(qn + EPS), ks = 1.0f / std::sqrt(kn + EPS);
+    for (int d = 0; d < HK; ++d) {
+      q[d] *= qs;
+      k[d] *= ks;
+    }
+    // decay / beta (src/engine.cpp:3277-3281)
+    const float alpha = bf16_to_f32(proj[CONV_CH + 4096 + vh]);
+    const float braw = bf16_to_f32(proj[CONV_CH + 4096 + VH + vh]);
+    const float biased = alpha + dt_bias[vh];
+    const float sp = (biased > 20.0f) ? biased : std::log(1.0f + mexp(biased, mode));
+    const float decay = std::exp(sp * ssm_a[vh]);
+    const float beta = msigmoid(braw, mode);
+    // delta rule (src/engine.cpp:3284-3305)
+    float* sh = state + (int64_t)vh * HV * HK;
+    float o[HV];
+    for (int i = 0; i < HV; ++i) {
+      float* row = sh + i * HK;
+      float sk = 0.0f;
+      for (int j = 0; j < HK; ++j) {
+        row[j] *= decay;
+        sk += row[j] * k[j];
+      }
+      const float dd = beta * (v[i] - sk);
+      float acc = 0.0f;
+      for (int j = 0; j < HK; ++j) {
+        row[j] += k[j] * dd;
+        acc += row[j] * q[j];
+      }
+      o[i] = acc * SSM_SCALE;
+    }
+    // gated RMSNorm (src/engine.cpp:3307-3322)
+    float ss = 0.0f;
+    for (int d = 0; d < HV; ++d) ss += o[d] * o[d];
+    const float rms = 1.0f / std::sqrt(ss / HV + EPS);
+    for (int d = 0; d < HV; ++d) {
+      zf[d] = bf16_to_f32(proj[CONV_CH + vh * HV + d]);
+      out[vh * HV + d] = (o[d] * rms) * ssm_norm[d] * msilu(zf[d], mode);
+    }
+  }
+}
+
+// conv1d + SiLU + history shift (src/engine.cpp:3204-3234).
+static void gdn_conv(const uint16_t* proj, float* conv, const float* w, float* conv_out, int mode) {
+  const float* s0 = conv;
+  const float* s1 = conv + CONV_CH;
+  const float* s2 = conv + 2 * CONV_CH;
+  for (int c = 0; c < CONV_CH; ++c) {
+    const float x = bf16_to_f32(proj[c]);
+    float y = s0[c] * w[c];
+    y = std::fma(s1[c], w[CONV_CH + c], y);
+    y = std::fma(s2[c], w[2 * CONV_CH + c], y);
+    y = std::fma(x, w[3 * CONV_CH + c], y);
+    conv_out[c] = msilu(y, mode);
+  }
+  std::memmove(conv, conv + CONV_CH, 2 * CONV_CH * sizeof(float));
+  for (int c = 0; c < CONV_CH; ++c) conv[2 * CONV_CH + c] = bf16_to_f32(proj[c]);
+}
+
+void qo_gdn_decode(const uint16_t* proj, float* state, float* conv, const float* conv_w,
+                   const float* ssm_a, const float* dt_bias, const float* ssm_norm, float* out,
+                   int mode) {
+  std::vector<float> conv_out(CONV_CH);
+  gdn_conv(proj, conv, conv_w, conv_out.data(), mode);
+  gdn_heads(proj, state, ssm_a, dt_bias, ssm_norm, out, mode, 0, VH, conv_out.data());
+}
+
+// ------------------------------------------------- threaded CPU baseline
+
+// A batch of independent sequences, threaded over (sequence x v-head) units
+// like the reference's WorkerPool over v-heads (src/engine.cpp:1630-1691,
+// 3326-3327).  Arrays are per-sequence contiguous.
+void qo_gdn_decode_batch(int n_seq, const uint16_t* proj, float* state, float* conv,
+                         const float* conv_w, const float* ssm_a, const float* dt_bias,
+                         const float* ssm_norm, float* out, int mode, int n_threads) {
+  std::vector<float> conv_out((int64_t)n_seq * CONV_CH);
+  for (int s = 0; s < n_seq; ++s)
+    gdn_conv(proj + (int64_t)s * GDN_PROJ, conv + (int64_t)s * 3 * CONV_CH, conv_w,
+             conv_out.data() + (int64_t)s * CONV_CH, mode);
+  const int units = n_seq * VH;
+  std::atomic<int> next{0};
+  auto work = [&]() {
+    for (int u; (u = next.fetch_add(1)) < units;) {
+      const int s = u / VH, vh = u % VH;
+      gdn_heads(proj + (int64_t)s * GDN_PROJ, state + (int64_t)s * VH * HV * HK, ssm_a, dt_bias,
+                ssm_norm, out + (int64_t)s * 4096, mode, vh, vh + 1,
+                conv_out.data() + (int64_t)s * CONV_CH);
+    }
+  };
+  std::vector<std::thread> th;
+  for (int t = 1; t < n_threads; ++t) th.emplace_back(work);
+  work();
+  for (auto& t : th) t.join();
+}
+
+// Attention for a batch of sequences at positions pos[s] with contiguous
+// per-sequence caches of capacity cap positions, threaded over sequences.
+void qo_attn_decode_batch(int n_seq, const uint16_t* proj, const float* q_norm,
+                          const float* k_norm, const int32_t* pos, uint16_t* k_cache,
+                          uint16_t* v_cache, int64_t cap, float* out, int mode, int n_threads) {
+  std::atomic<int> next{0};
+  auto work = [&]() {
+    for (int s; (s = next.fetch_add(1)) < n_seq;)
+      qo_attn_decode(proj + (int64_t)s * ATTN_PROJ, q_norm, k_norm, pos[s],
+                     k_cache + s * cap * KV_DIM, v_cache + s * cap * KV_DIM, out + (int64_t)s * 4096,
+                     mode);
+  };
+  std::vector<std::thread> th;
+  for (int t = 1; t < n_threads; ++t) th.emplace_back(work);
+  work();
+  for (auto& t : th) t.join();
+}
+
+// --------------------------------------------------------- prefix rule
+
+// The reference's prefix decision (src/engine.cpp:4058-4080): returns the
+// number of prompt tokens that are reused; *reset = 1 when the cached state
+// must be discarded first.
+int qo_prefix_decide(const int32_t* cached, int n_cached, const int32_t* prompt, int n_prompt,
+                     int* reset) {
+  int prefix = 0;
+  const int check = std::min(n_cached, n_prompt);
+  while (prefix < check && prompt[prefix] == cached[prefix]) ++prefix;
+  *reset = 0;
+  if (prefix < n_cached) {
+    *reset = 1;
+    prefix = 0;
+  }
+  if (prefix >= n_prompt) {
+    *reset = 1;
+    prefix = 0;
+  }
+  return prefix;
+}
+
+}  // extern "C"

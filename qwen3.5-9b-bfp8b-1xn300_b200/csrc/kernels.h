@@ -1,0 +1,92 @@
+// kernels.h — launch interface between the host context (qcache.cu) and the
+// device kernels.  Plain structs of device pointers and sizes.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace qc {
+
+// Gated-DeltaNet decode step (gdn_decode.cu).
+struct GdnArgs {
+  const uint16_t* proj;      // [n][12352] bf16
+  uint16_t* out;             // [n][4096] bf16
+  float* state;              // this layer's state of slot 0; slot s at + s * state_stride
+  uint16_t* ring;            // this layer's conv ring [4][8192] bf16 of slot 0
+  int64_t state_stride;      // floats between slots
+  int64_t ring_stride;       // elements between slots
+  const float* conv_w;       // [4][8192]
+  const float* ssm_a;        // [32]
+  const float* dt_bias;      // [32]
+  const float* ssm_norm;     // [128]
+  const int32_t* slots;      // [n]
+  const int32_t* pos;        // [n]
+  int32_t n;
+  int* err;
+};
+cudaError_t launch_gdn_decode(const GdnArgs& a, cudaStream_t s);
+
+// Split-K paged attention (attn_decode.cu).
+struct AttnArgs {
+  const uint16_t* proj;      // [n][10240] bf16
+  uint16_t* k_pool;          // this layer: [max_pages][4][64][256] bf16
+  uint16_t* v_pool;
+  const int32_t* page_table; // [max_seqs][pt_stride]
+  int32_t pt_stride;
+  int32_t max_pages;
+  const int32_t* slots;      // [n]
+  const int32_t* pos;        // [n]  position of the new token
+  const int32_t* seg;        // [n + 1] prefix sums of page-heads (4 * pages processed)
+  const int32_t* page0;      // [n]  first page processed (0 for a full decode)
+  const int32_t* append;     // [n]  1: this call appends the new token and attends to it
+  const float* q_norm;       // [256]
+  const float* k_norm;       // [256]
+  const float* rope_cos;     // [max_ctx][32]
+  const float* rope_sin;
+  float* part_m;             // [slots][4] (log2 domain)
+  float* part_l;             // [slots][4]
+  float* part_o;             // [slots][4][256]
+  int32_t n;
+  int32_t total;             // page-heads in the batch
+  int32_t per;               // page-heads per CTA
+  int32_t grid;              // CTAs
+  int* err;
+};
+// Combine the partials of each (sequence, kv-head) pair, apply the gate and
+// store bf16 (attn_decode.cu).
+struct CombineArgs {
+  const uint16_t* proj;
+  uint16_t* out;             // [n][4096]
+  const int32_t* seg;
+  const float* part_m;
+  const float* part_l;
+  const float* part_o;
+  int32_t n;
+  int32_t per;
+};
+cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, cudaStream_t s);
+int attn_smem_bytes();
+
+// Copies (kv_copy.cu).
+// Scatter / gather of positions [pos0, pos0 + n) of one sequence between a
+// contiguous [n][4][256] array and the paged pool of one layer.
+cudaError_t launch_kv_scatter(uint16_t* k_pool, uint16_t* v_pool, const int32_t* page_row,
+                              int32_t pos0, int32_t n, const uint16_t* k, const uint16_t* v,
+                              int32_t max_pages, int* err, cudaStream_t s);
+cudaError_t launch_kv_gather(const uint16_t* k_pool, const uint16_t* v_pool,
+                             const int32_t* page_row, int32_t pos0, int32_t n, uint16_t* k,
+                             uint16_t* v, int32_t max_pages, int* err, cudaStream_t s);
+// Generic batched copy: n_jobs jobs of (src, dst, bytes), bytes and both
+// addresses multiples of 16; jobs split into chunks of `chunk` bytes.
+struct CopyJob {
+  const void* src;
+  void* dst;
+  int64_t bytes;
+};
+cudaError_t launch_copy_jobs(const CopyJob* jobs_dev, int32_t n_jobs, const int64_t* chunk_start_dev,
+                             int64_t n_chunks, int32_t chunk, cudaStream_t s);
+// Conv ring <-> oldest-first [3][8192] history of one layer of one sequence.
+cudaError_t launch_ring_to_hist(const uint16_t* ring, int32_t pos, uint16_t* hist, cudaStream_t s);
+cudaError_t launch_hist_to_ring(const uint16_t* hist, int32_t pos, uint16_t* ring, cudaStream_t s);
+
+}  // namespace qc

@@ -1,0 +1,963 @@
+// qcache.cu — host side of the cache path: the context behind include/qcache.h.
+//
+// Owns the device pools (paged bf16 KV, DeltaNet state, conv rings, prefix
+// snapshots), the host page allocator with refcounts, the per-sequence page
+// tables and token histories, and the hashed prefix table.  Every device
+// operation is a kernel or copy enqueued on the caller's stream; there is no
+// host fallback for any computation.
+//
+// Reference correspondence (src/engine.cpp): the globals g_k_cache/g_v_cache,
+// g_ssm_state, g_conv_state, g_cached_tokens (79-97) become per-sequence
+// device state here; reset_state (4164-4176) is qc_seq_reset; the prefix rule
+// of generate() (4058-4080) is qc_seq_match_prefix.
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/qcache.h"
+#include "kernels.h"
+
+using qc::CopyJob;
+
+namespace {
+
+constexpr int HD = QC_HEAD_DIM;
+constexpr int PAGE = QC_PAGE;
+constexpr int64_t PAGE_ELEMS = (int64_t)QC_N_HEAD_KV * PAGE * HD;       // per layer, K or V
+constexpr int64_t RING_ELEMS = 4LL * QC_CONV_CH;                        // [4][8192]
+constexpr int64_t HIST_ELEMS = 3LL * QC_CONV_CH;                        // [3][8192]
+constexpr int COPY_CHUNK = 64 * 1024;
+constexpr int STAGING_SLOTS = 4;
+
+struct Seq {
+  bool live = false;
+  int32_t len = 0;
+  std::vector<int32_t> pages;
+  std::vector<int32_t> tokens;
+  bool dirty = false;  // page-table row differs from the device copy
+};
+
+struct Entry {
+  bool live = false;
+  int32_t P = 0;
+  std::vector<int32_t> tokens;
+  std::vector<int32_t> pages;  // full pages shared, tail page owned
+  int32_t snap = -1;
+  uint64_t key = 0;            // chain hash after the last full page
+};
+
+}  // namespace
+
+struct qc_ctx {
+  qc_config cfg{};
+  int device = QC_DEVICE_NONE;
+  bool host_only = true;
+  int nsm = 148;
+  std::string err;
+  int32_t pt_stride = 0;  // page-table row capacity (pages per sequence)
+
+  // device pools
+  uint16_t* k_pool = nullptr;   // [n_attn][max_pages][4][64][256]
+  uint16_t* v_pool = nullptr;
+  float* state = nullptr;       // [max_seqs][n_gdn][32][128][128]
+  uint16_t* ring = nullptr;     // [max_seqs][n_gdn][4][8192]
+  float* snap_state = nullptr;  // [max_snapshots][n_gdn][32][128][128]
+  uint16_t* snap_hist = nullptr;// [max_snapshots][n_gdn][3][8192]
+  float* q_norm = nullptr;      // [n_attn][256]
+  float* k_norm = nullptr;
+  float* ssm_a = nullptr;       // [n_gdn][32]
+  float* dt_bias = nullptr;     // [n_gdn][32]
+  float* ssm_norm = nullptr;    // [n_gdn][128]
+  float* conv_w = nullptr;      // [n_gdn][4][8192]
+  float* rope_cos = nullptr;    // [max_ctx][32]
+  float* rope_sin = nullptr;
+  int32_t* page_table = nullptr;// [max_seqs][pt_stride]
+  int32_t* desc = nullptr;      // batch: slots | pos | seg | page0 | append
+  float* part_m = nullptr;
+  float* part_l = nullptr;
+  float* part_o = nullptr;
+  int32_t part_slots = 0;
+  CopyJob* jobs = nullptr;
+  int64_t* chunk_start = nullptr;
+  int32_t job_cap = 0;
+  int* dev_err = nullptr;
+
+  // pinned staging ring for host -> device uploads
+  char* stage[STAGING_SLOTS] = {};
+  cudaEvent_t stage_ev[STAGING_SLOTS] = {};
+  size_t stage_cap = 0;
+  int stage_next = 0;
+
+  // host bookkeeping
+  std::vector<Seq> seqs;
+  std::vector<int32_t> page_ref;
+  std::vector<int32_t> free_pages;
+  std::vector<int32_t> h_page_table;
+  std::vector<Entry> entries;
+  std::unordered_map<uint64_t, std::vector<int32_t>> index;
+  std::vector<int32_t> free_snaps;
+
+  // current decode batch
+  bool in_step = false;
+  std::vector<int32_t> b_seq, b_pos, b_seg, b_tok;
+  bool b_has_tok = false;
+  int32_t b_total = 0, b_per = 0, b_grid = 0;
+  int64_t last_restore_bytes = 0;
+};
+
+namespace {
+
+int fail(qc_ctx* c, int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (c) c->err = buf;
+  return code;
+}
+
+#define QC_CUDA(c, call)                                                              \
+  do {                                                                                \
+    cudaError_t e_ = (call);                                                          \
+    if (e_ != cudaSuccess)                                                            \
+      return fail((c), QC_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_),  \
+                  __FILE__, __LINE__);                                                \
+  } while (0)
+
+#define QC_NEED_DEVICE(c) \
+  do {                    \
+    if ((c)->host_only) return fail((c), QC_ERR_NODEVICE, "host-only context: no device work"); \
+  } while (0)
+
+bool valid_seq(const qc_ctx* c, int32_t s) {
+  return s >= 0 && s < (int32_t)c->seqs.size() && c->seqs[s].live;
+}
+
+// ---- page allocator
+int32_t page_alloc(qc_ctx* c) {
+  if (c->free_pages.empty()) return -1;
+  const int32_t p = c->free_pages.back();
+  c->free_pages.pop_back();
+  c->page_ref[p] = 1;
+  return p;
+}
+void page_decref(qc_ctx* c, int32_t p) {
+  if (--c->page_ref[p] == 0) c->free_pages.push_back(p);
+}
+
+void set_row(qc_ctx* c, int32_t s) {
+  Seq& q = c->seqs[s];
+  int32_t* row = &c->h_page_table[(size_t)s * c->pt_stride];
+  std::fill(row, row + c->pt_stride, -1);
+  std::copy(q.pages.begin(), q.pages.end(), row);
+  q.dirty = true;
+}
+
+// ---- pinned staging
+// Returns a pinned buffer whose previous upload has completed.
+int stage_acquire(qc_ctx* c, size_t bytes, char** out, int* idx) {
+  if (bytes > c->stage_cap)
+    return fail(c, QC_ERR_ARG, "upload of %zu bytes exceeds staging capacity %zu", bytes,
+                c->stage_cap);
+  const int i = c->stage_next;
+  c->stage_next = (i + 1) % STAGING_SLOTS;
+  QC_CUDA(c, cudaEventSynchronize(c->stage_ev[i]));
+  *out = c->stage[i];
+  *idx = i;
+  return QC_OK;
+}
+int stage_release(qc_ctx* c, int i, cudaStream_t s) {
+  QC_CUDA(c, cudaEventRecord(c->stage_ev[i], s));
+  return QC_OK;
+}
+
+// Upload every dirty page-table row.
+int sync_rows(qc_ctx* c, cudaStream_t s) {
+  for (size_t i = 0; i < c->seqs.size(); ++i) {
+    Seq& q = c->seqs[i];
+    if (!q.live || !q.dirty) continue;
+    const size_t bytes = (size_t)c->pt_stride * sizeof(int32_t);
+    char* buf = nullptr;
+    int si = 0;
+    if (int rc0 = stage_acquire(c, bytes, &buf, &si)) return rc0;
+    std::memcpy(buf, &c->h_page_table[i * c->pt_stride], bytes);
+    QC_CUDA(c, cudaMemcpyAsync(c->page_table + i * c->pt_stride, buf, bytes,
+                               cudaMemcpyHostToDevice, s));
+    int rc = stage_release(c, si, s);
+    if (rc) return rc;
+    q.dirty = false;
+  }
+  return QC_OK;
+}
+
+// Run a list of copy jobs on the device (one launch).
+int run_jobs(qc_ctx* c, const std::vector<CopyJob>& jobs, cudaStream_t s, int64_t* bytes_out) {
+  if (jobs.empty()) return QC_OK;
+  if ((int32_t)jobs.size() > c->job_cap)
+    return fail(c, QC_ERR_ARG, "%zu copy jobs exceed capacity %d", jobs.size(), c->job_cap);
+  std::vector<int64_t> starts(jobs.size() + 1, 0);
+  int64_t total = 0;
+  for (size_t j = 0; j < jobs.size(); ++j) {
+    starts[j + 1] = starts[j] + (jobs[j].bytes + COPY_CHUNK - 1) / COPY_CHUNK;
+    total += jobs[j].bytes;
+  }
+  const size_t jb = jobs.size() * sizeof(CopyJob), sb = starts.size() * sizeof(int64_t);
+  char* buf = nullptr;
+  int si = 0;
+  if (int rc0 = stage_acquire(c, jb + sb, &buf, &si)) return rc0;
+  std::memcpy(buf, jobs.data(), jb);
+  std::memcpy(buf + jb, starts.data(), sb);
+  QC_CUDA(c, cudaMemcpyAsync(c->jobs, buf, jb, cudaMemcpyHostToDevice, s));
+  QC_CUDA(c, cudaMemcpyAsync(c->chunk_start, buf + jb, sb, cudaMemcpyHostToDevice, s));
+  int rc = stage_release(c, si, s);
+  if (rc) return rc;
+  QC_CUDA(c, qc::launch_copy_jobs(c->jobs, (int32_t)jobs.size(), c->chunk_start, starts.back(),
+                                  COPY_CHUNK, s));
+  if (bytes_out) *bytes_out += 2 * total;
+  return QC_OK;
+}
+
+// Copy jobs duplicating page src into page dst for every attention layer.
+void page_copy_jobs(const qc_ctx* c, int32_t src, int32_t dst, std::vector<CopyJob>& jobs) {
+  const int64_t bytes = PAGE_ELEMS * 2;
+  for (int l = 0; l < c->cfg.n_attn_layers; ++l) {
+    const int64_t base = (int64_t)l * c->cfg.max_pages * PAGE_ELEMS;
+    jobs.push_back({c->k_pool + base + src * PAGE_ELEMS, c->k_pool + base + dst * PAGE_ELEMS, bytes});
+    jobs.push_back({c->v_pool + base + src * PAGE_ELEMS, c->v_pool + base + dst * PAGE_ELEMS, bytes});
+  }
+}
+
+float* slot_state(const qc_ctx* c, int32_t s, int layer) {
+  return c->state + ((int64_t)s * c->cfg.n_gdn_layers + layer) * QC_GDN_STATE;
+}
+uint16_t* slot_ring(const qc_ctx* c, int32_t s, int layer) {
+  return c->ring + ((int64_t)s * c->cfg.n_gdn_layers + layer) * RING_ELEMS;
+}
+float* snap_state_ptr(const qc_ctx* c, int32_t snap) {
+  return c->snap_state + (int64_t)snap * c->cfg.n_gdn_layers * QC_GDN_STATE;
+}
+uint16_t* snap_hist_ptr(const qc_ctx* c, int32_t snap, int layer) {
+  return c->snap_hist + ((int64_t)snap * c->cfg.n_gdn_layers + layer) * HIST_ELEMS;
+}
+
+// ---- prefix hashing: 64-bit mix of the previous hash and a page of tokens.
+constexpr uint64_t HASH_SEED = 0x9e3779b97f4a7c15ull;
+uint64_t mix64(uint64_t x) {
+  x ^= x >> 30;
+  x *= 0xbf58476d1ce4e5b9ull;
+  x ^= x >> 27;
+  x *= 0x94d049bb133111ebull;
+  x ^= x >> 31;
+  return x;
+}
+uint64_t page_hash(uint64_t prev, const int32_t* t) {
+  uint64_t h = mix64(prev ^ 0x51afd7ed558ccd6dull);
+  for (int i = 0; i < PAGE; ++i) h = mix64(h ^ (uint32_t)t[i]) + (uint64_t)i;
+  return h;
+}
+
+int free_seq_pages(qc_ctx* c, int32_t s) {
+  Seq& q = c->seqs[s];
+  for (int32_t p : q.pages) page_decref(c, p);
+  q.pages.clear();
+  set_row(c, s);
+  return QC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+// Message of a failed qc_create (which returns no context) on this thread.
+static thread_local std::string g_create_err;
+
+const char* qc_last_error(const qc_ctx* ctx) { return ctx ? ctx->err.c_str() : g_create_err.c_str(); }
+
+int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
+  if (!cfg || !out) return QC_ERR_ARG;
+  *out = nullptr;
+  if (cfg->n_attn_layers <= 0 || cfg->n_gdn_layers < 0 || cfg->max_seqs <= 0 ||
+      cfg->max_pages <= 0 || cfg->max_ctx <= 0 || cfg->max_batch <= 0 ||
+      cfg->max_snapshots < 0 || cfg->max_batch > cfg->max_seqs)
+    return QC_ERR_ARG;
+  qc_ctx* c = new qc_ctx();
+  c->cfg = *cfg;
+  c->device = device;
+  c->host_only = true;  // becomes false once the device pools exist
+  c->pt_stride = (cfg->max_ctx + PAGE - 1) / PAGE + 1;
+  c->seqs.resize(cfg->max_seqs);
+  c->page_ref.assign(cfg->max_pages, 0);
+  for (int32_t p = cfg->max_pages - 1; p >= 0; --p) c->free_pages.push_back(p);
+  c->h_page_table.assign((size_t)cfg->max_seqs * c->pt_stride, -1);
+  c->entries.reserve(64);
+  for (int32_t s = cfg->max_snapshots - 1; s >= 0; --s) c->free_snaps.push_back(s);
+  if (device == QC_DEVICE_NONE) {
+    *out = c;
+    return QC_OK;
+  }
+
+  // On failure the partial context is released and the message kept for
+  // qc_last_error(NULL).
+  auto cuda_fail = [&](cudaError_t e, const char* what) {
+    char buf[256];
+    snprintf(buf, sizeof(buf), "qc_create: %s: %s", what, cudaGetErrorString(e));
+    g_create_err = buf;
+    c->host_only = false;
+    qc_destroy(c);
+    return e == cudaErrorMemoryAllocation ? QC_ERR_OOM : QC_ERR_CUDA;
+  };
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  cudaDeviceGetAttribute(&c->nsm, cudaDevAttrMultiProcessorCount, device);
+  const int na = cfg->n_attn_layers, ng = cfg->n_gdn_layers;
+  const int64_t pool = (int64_t)na * cfg->max_pages * PAGE_ELEMS;
+  c->part_slots = 4 * cfg->max_batch + c->nsm + 8;
+  c->job_cap = cfg->max_batch * (1 + 3 * std::max(ng, 1) + 2 * na) + 64;
+  struct A { void** p; size_t bytes; const char* what; };
+  const A allocs[] = {
+      {(void**)&c->k_pool, (size_t)pool * 2, "k_pool"},
+      {(void**)&c->v_pool, (size_t)pool * 2, "v_pool"},
+      {(void**)&c->state, (size_t)cfg->max_seqs * std::max(ng, 1) * QC_GDN_STATE * 4, "state"},
+      {(void**)&c->ring, (size_t)cfg->max_seqs * std::max(ng, 1) * RING_ELEMS * 2, "ring"},
+      {(void**)&c->snap_state, (size_t)std::max(cfg->max_snapshots, 1) * std::max(ng, 1) * QC_GDN_STATE * 4, "snap_state"},
+      {(void**)&c->snap_hist, (size_t)std::max(cfg->max_snapshots, 1) * std::max(ng, 1) * HIST_ELEMS * 2, "snap_hist"},
+      {(void**)&c->q_norm, (size_t)na * HD * 4, "q_norm"},
+      {(void**)&c->k_norm, (size_t)na * HD * 4, "k_norm"},
+      {(void**)&c->ssm_a, (size_t)std::max(ng, 1) * 32 * 4, "ssm_a"},
+      {(void**)&c->dt_bias, (size_t)std::max(ng, 1) * 32 * 4, "dt_bias"},
+      {(void**)&c->ssm_norm, (size_t)std::max(ng, 1) * 128 * 4, "ssm_norm"},
+      {(void**)&c->conv_w, (size_t)std::max(ng, 1) * 4 * QC_CONV_CH * 4, "conv_w"},
+      {(void**)&c->rope_cos, (size_t)cfg->max_ctx * 32 * 4, "rope_cos"},
+      {(void**)&c->rope_sin, (size_t)cfg->max_ctx * 32 * 4, "rope_sin"},
+      {(void**)&c->page_table, (size_t)cfg->max_seqs * c->pt_stride * 4, "page_table"},
+      {(void**)&c->desc, (size_t)(5 * cfg->max_batch + 8) * 4, "desc"},
+      {(void**)&c->part_m, (size_t)c->part_slots * 4 * 4, "part_m"},
+      {(void**)&c->part_l, (size_t)c->part_slots * 4 * 4, "part_l"},
+      {(void**)&c->part_o, (size_t)c->part_slots * 4 * HD * 4, "part_o"},
+      {(void**)&c->jobs, (size_t)c->job_cap * sizeof(CopyJob), "jobs"},
+      {(void**)&c->chunk_start, (size_t)(c->job_cap + 1) * 8, "chunk_start"},
+      {(void**)&c->dev_err, 16, "dev_err"},
+  };
+  for (const A& a : allocs) {
+    e = cudaMalloc(a.p, a.bytes);
+    if (e != cudaSuccess) return cuda_fail(e, a.what);
+  }
+  // zeroed state so that a fresh sequence equals reset_state()
+  if ((e = cudaMemset(c->state, 0, (size_t)cfg->max_seqs * std::max(ng, 1) * QC_GDN_STATE * 4)) ||
+      (e = cudaMemset(c->ring, 0, (size_t)cfg->max_seqs * std::max(ng, 1) * RING_ELEMS * 2)) ||
+      (e = cudaMemset(c->page_table, 0xff, (size_t)cfg->max_seqs * c->pt_stride * 4)) ||
+      (e = cudaMemset(c->dev_err, 0, 16)))
+    return cuda_fail(e, "cudaMemset");
+
+  // RoPE table, the formula of precompute_rope (src/engine.cpp:2408-2420)
+  {
+    std::vector<float> cs((size_t)cfg->max_ctx * 32), sn((size_t)cfg->max_ctx * 32);
+    float freq[32];
+    for (int p = 0; p < 32; ++p) freq[p] = 1.0f / powf(10000000.0f, 2.0f * p / QC_ROPE_DIM);
+    for (int pos = 0; pos < cfg->max_ctx; ++pos)
+      for (int p = 0; p < 32; ++p) {
+        const float theta = pos * freq[p];
+        cs[(size_t)pos * 32 + p] = cosf(theta);
+        sn[(size_t)pos * 32 + p] = sinf(theta);
+      }
+    if ((e = cudaMemcpy(c->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice)) ||
+        (e = cudaMemcpy(c->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice)))
+      return cuda_fail(e, "rope upload");
+  }
+  c->stage_cap = std::max<size_t>((size_t)(5 * cfg->max_batch + 8) * 4 +
+                                      (size_t)c->pt_stride * 4,
+                                  (size_t)c->job_cap * (sizeof(CopyJob) + 8) + 8);
+  for (int i = 0; i < STAGING_SLOTS; ++i) {
+    if ((e = cudaMallocHost((void**)&c->stage[i], c->stage_cap)) ||
+        (e = cudaEventCreateWithFlags(&c->stage_ev[i], cudaEventDisableTiming)))
+      return cuda_fail(e, "staging");
+  }
+  c->host_only = false;
+  *out = c;
+  return QC_OK;
+}
+
+void qc_destroy(qc_ctx* c) {
+  if (!c) return;
+  if (!c->host_only) {
+    cudaSetDevice(c->device);
+    cudaDeviceSynchronize();
+    void* ptrs[] = {c->k_pool, c->v_pool, c->state, c->ring, c->snap_state, c->snap_hist,
+                    c->q_norm, c->k_norm, c->ssm_a, c->dt_bias, c->ssm_norm, c->conv_w,
+                    c->rope_cos, c->rope_sin, c->page_table, c->desc, c->part_m, c->part_l,
+                    c->part_o, c->jobs, c->chunk_start, c->dev_err};
+    for (void* p : ptrs)
+      if (p) cudaFree(p);
+    for (int i = 0; i < STAGING_SLOTS; ++i) {
+      if (c->stage[i]) cudaFreeHost(c->stage[i]);
+      if (c->stage_ev[i]) cudaEventDestroy(c->stage_ev[i]);
+    }
+  }
+  delete c;
+}
+
+int qc_check_device(qc_ctx* c, qc_stream stream) {
+  if (!c) return QC_ERR_ARG;
+  QC_NEED_DEVICE(c);
+  QC_CUDA(c, cudaStreamSynchronize((cudaStream_t)stream));
+  int code = 0;
+  QC_CUDA(c, cudaMemcpy(&code, c->dev_err, 4, cudaMemcpyDeviceToHost));
+  QC_CUDA(c, cudaMemset(c->dev_err, 0, 4));
+  if (code) return fail(c, code, "device reported error %d", code);
+  return QC_OK;
+}
+
+int qc_set_attn_params(qc_ctx* c, int layer, const float* q_norm, const float* k_norm) {
+  if (!c || !q_norm || !k_norm) return QC_ERR_ARG;
+  if (layer < 0 || layer >= c->cfg.n_attn_layers) return fail(c, QC_ERR_ARG, "attn layer %d", layer);
+  QC_NEED_DEVICE(c);
+  QC_CUDA(c, cudaMemcpy(c->q_norm + layer * HD, q_norm, HD * 4, cudaMemcpyHostToDevice));
+  QC_CUDA(c, cudaMemcpy(c->k_norm + layer * HD, k_norm, HD * 4, cudaMemcpyHostToDevice));
+  return QC_OK;
+}
+
+int qc_set_gdn_params(qc_ctx* c, int layer, const float* ssm_a, const float* dt_bias,
+                      const float* ssm_norm, const float* conv_w) {
+  if (!c || !ssm_a || !dt_bias || !ssm_norm || !conv_w) return QC_ERR_ARG;
+  if (layer < 0 || layer >= c->cfg.n_gdn_layers) return fail(c, QC_ERR_ARG, "gdn layer %d", layer);
+  QC_NEED_DEVICE(c);
+  QC_CUDA(c, cudaMemcpy(c->ssm_a + layer * 32, ssm_a, 32 * 4, cudaMemcpyHostToDevice));
+  QC_CUDA(c, cudaMemcpy(c->dt_bias + layer * 32, dt_bias, 32 * 4, cudaMemcpyHostToDevice));
+  QC_CUDA(c, cudaMemcpy(c->ssm_norm + layer * 128, ssm_norm, 128 * 4, cudaMemcpyHostToDevice));
+  QC_CUDA(c, cudaMemcpy(c->conv_w + (int64_t)layer * 4 * QC_CONV_CH, conv_w, 4 * QC_CONV_CH * 4,
+                        cudaMemcpyHostToDevice));
+  return QC_OK;
+}
+
+// ----------------------------------------------------------------- sequences
+
+int qc_seq_alloc(qc_ctx* c, int32_t* seq) {
+  if (!c || !seq) return QC_ERR_ARG;
+  for (int32_t s = 0; s < (int32_t)c->seqs.size(); ++s) {
+    if (!c->seqs[s].live) {
+      c->seqs[s] = Seq();
+      c->seqs[s].live = true;
+      set_row(c, s);
+      *seq = s;
+      return QC_OK;
+    }
+  }
+  return fail(c, QC_ERR_OOM, "no free sequence slot (max_seqs %d)", c->cfg.max_seqs);
+}
+
+int qc_seq_reset(qc_ctx* c, int32_t s, qc_stream stream) {
+  if (!c) return QC_ERR_ARG;
+  if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
+  if (c->in_step) return fail(c, QC_ERR_ARG, "reset inside a decode step");
+  free_seq_pages(c, s);
+  c->seqs[s].len = 0;
+  c->seqs[s].tokens.clear();
+  if (!c->host_only) {
+    const int ng = c->cfg.n_gdn_layers;
+    if (ng > 0) {
+      cudaStream_t st = (cudaStream_t)stream;
+      QC_CUDA(c, cudaMemsetAsync(slot_state(c, s, 0), 0, (size_t)ng * QC_GDN_STATE * 4, st));
+      QC_CUDA(c, cudaMemsetAsync(slot_ring(c, s, 0), 0, (size_t)ng * RING_ELEMS * 2, st));
+    }
+  }
+  return QC_OK;
+}
+
+int qc_seq_free(qc_ctx* c, int32_t s) {
+  if (!c) return QC_ERR_ARG;
+  if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
+  if (c->in_step) return fail(c, QC_ERR_ARG, "free inside a decode step");
+  free_seq_pages(c, s);
+  c->seqs[s] = Seq();
+  return QC_OK;
+}
+
+int qc_seq_len(const qc_ctx* c, int32_t s, int32_t* len) {
+  if (!c || !len || !valid_seq(c, s)) return QC_ERR_ARG;
+  *len = c->seqs[s].len;
+  return QC_OK;
+}
+
+int qc_seq_pages(const qc_ctx* c, int32_t s, int32_t* pages, int32_t cap, int32_t* n_pages) {
+  if (!c || !n_pages || !valid_seq(c, s)) return QC_ERR_ARG;
+  const Seq& q = c->seqs[s];
+  *n_pages = (int32_t)q.pages.size();
+  if (pages)
+    for (int32_t i = 0; i < std::min(cap, *n_pages); ++i) pages[i] = q.pages[i];
+  return QC_OK;
+}
+
+int qc_seq_reserve(qc_ctx* c, int32_t s, int32_t new_len) {
+  if (!c) return QC_ERR_ARG;
+  if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
+  if (c->in_step) return fail(c, QC_ERR_ARG, "reserve inside a decode step");
+  Seq& q = c->seqs[s];
+  if (new_len < q.len || new_len > c->cfg.max_ctx)
+    return fail(c, QC_ERR_ARG, "reserve %d: length %d, max_ctx %d", new_len, q.len, c->cfg.max_ctx);
+  const int32_t need = (new_len + PAGE - 1) / PAGE;
+  const size_t before = q.pages.size();
+  while ((int32_t)q.pages.size() < need) {
+    const int32_t p = page_alloc(c);
+    if (p < 0) {
+      while (q.pages.size() > before) {
+        page_decref(c, q.pages.back());
+        q.pages.pop_back();
+      }
+      return fail(c, QC_ERR_OOM, "KV page pool exhausted (%d pages)", c->cfg.max_pages);
+    }
+    q.pages.push_back(p);
+  }
+  q.len = new_len;
+  set_row(c, s);
+  return QC_OK;
+}
+
+static int kv_check(qc_ctx* c, int32_t s, int layer, int32_t pos0, int32_t n, bool writing) {
+  if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
+  if (layer < 0 || layer >= c->cfg.n_attn_layers) return fail(c, QC_ERR_ARG, "attn layer %d", layer);
+  const Seq& q = c->seqs[s];
+  if (pos0 < 0 || n < 0 || (int64_t)pos0 + n > (int64_t)q.pages.size() * PAGE)
+    return fail(c, QC_ERR_ARG, "positions [%d, %d) not backed (%zu pages)", pos0, pos0 + n,
+                q.pages.size());
+  if (writing)
+    for (int32_t pg = pos0 / PAGE; n > 0 && pg <= (pos0 + n - 1) / PAGE; ++pg)
+      if (c->page_ref[q.pages[pg]] > 1)
+        return fail(c, QC_ERR_ARG, "page %d of sequence %d is shared (prefix cache)", pg, s);
+  return QC_OK;
+}
+
+int qc_kv_write(qc_ctx* c, int32_t s, int layer, int32_t pos0, int32_t n, const uint16_t* k,
+                const uint16_t* v, qc_stream stream) {
+  if (!c || !k || !v) return QC_ERR_ARG;
+  int rc = kv_check(c, s, layer, pos0, n, true);
+  if (rc) return rc;
+  QC_NEED_DEVICE(c);
+  cudaStream_t st = (cudaStream_t)stream;
+  if ((rc = sync_rows(c, st))) return rc;
+  const int64_t base = (int64_t)layer * c->cfg.max_pages * PAGE_ELEMS;
+  QC_CUDA(c, qc::launch_kv_scatter(c->k_pool + base, c->v_pool + base,
+                                   c->page_table + (int64_t)s * c->pt_stride, pos0, n, k, v,
+                                   c->cfg.max_pages, c->dev_err, st));
+  return QC_OK;
+}
+
+int qc_kv_read(qc_ctx* c, int32_t s, int layer, int32_t pos0, int32_t n, uint16_t* k,
+               uint16_t* v, qc_stream stream) {
+  if (!c || !k || !v) return QC_ERR_ARG;
+  int rc = kv_check(c, s, layer, pos0, n, false);
+  if (rc) return rc;
+  QC_NEED_DEVICE(c);
+  cudaStream_t st = (cudaStream_t)stream;
+  if ((rc = sync_rows(c, st))) return rc;
+  const int64_t base = (int64_t)layer * c->cfg.max_pages * PAGE_ELEMS;
+  QC_CUDA(c, qc::launch_kv_gather(c->k_pool + base, c->v_pool + base,
+                                  c->page_table + (int64_t)s * c->pt_stride, pos0, n, k, v,
+                                  c->cfg.max_pages, c->dev_err, st));
+  return QC_OK;
+}
+
+int qc_gdn_state_write(qc_ctx* c, int32_t s, int layer, const float* state,
+                       const uint16_t* conv, qc_stream stream) {
+  if (!c || !state || !conv) return QC_ERR_ARG;
+  if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
+  if (layer < 0 || layer >= c->cfg.n_gdn_layers) return fail(c, QC_ERR_ARG, "gdn layer %d", layer);
+  QC_NEED_DEVICE(c);
+  cudaStream_t st = (cudaStream_t)stream;
+  QC_CUDA(c, cudaMemcpyAsync(slot_state(c, s, layer), state, (size_t)QC_GDN_STATE * 4,
+                             cudaMemcpyDeviceToDevice, st));
+  QC_CUDA(c, qc::launch_hist_to_ring(conv, c->seqs[s].len, slot_ring(c, s, layer), st));
+  return QC_OK;
+}
+
+int qc_gdn_state_read(qc_ctx* c, int32_t s, int layer, float* state, uint16_t* conv,
+                      qc_stream stream) {
+  if (!c || !state || !conv) return QC_ERR_ARG;
+  if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
+  if (layer < 0 || layer >= c->cfg.n_gdn_layers) return fail(c, QC_ERR_ARG, "gdn layer %d", layer);
+  QC_NEED_DEVICE(c);
+  cudaStream_t st = (cudaStream_t)stream;
+  QC_CUDA(c, cudaMemcpyAsync(state, slot_state(c, s, layer), (size_t)QC_GDN_STATE * 4,
+                             cudaMemcpyDeviceToDevice, st));
+  QC_CUDA(c, qc::launch_ring_to_hist(slot_ring(c, s, layer), c->seqs[s].len, conv, st));
+  return QC_OK;
+}
+
+// --------------------------------------------------------------- decode step
+
+int qc_decode_begin(qc_ctx* c, const int32_t* seq_ids, int32_t n, const int32_t* tokens,
+                    qc_stream stream) {
+  if (!c || !seq_ids) return QC_ERR_ARG;
+  if (c->in_step) return fail(c, QC_ERR_ARG, "decode step already open");
+  if (n <= 0 || n > c->cfg.max_batch)
+    return fail(c, QC_ERR_ARG, "batch of %d (max_batch %d)", n, c->cfg.max_batch);
+  cudaStream_t st = (cudaStream_t)stream;
+  std::vector<CopyJob> cow;
+  std::vector<char> seen(c->seqs.size(), 0);
+  for (int32_t i = 0; i < n; ++i) {
+    const int32_t s = seq_ids[i];
+    if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
+    if (seen[s]) return fail(c, QC_ERR_ARG, "sequence %d twice in one batch", s);
+    seen[s] = 1;
+    if (c->seqs[s].len >= c->cfg.max_ctx)
+      return fail(c, QC_ERR_ARG, "sequence %d is full (max_ctx %d)", s, c->cfg.max_ctx);
+  }
+  for (int32_t i = 0; i < n; ++i) {
+    Seq& q = c->seqs[seq_ids[i]];
+    const int32_t pi = q.len / PAGE;
+    if (pi == (int32_t)q.pages.size()) {
+      const int32_t p = page_alloc(c);
+      if (p < 0) return fail(c, QC_ERR_OOM, "KV page pool exhausted (%d pages)", c->cfg.max_pages);
+      q.pages.push_back(p);
+      set_row(c, seq_ids[i]);
+    } else if (c->page_ref[q.pages[pi]] > 1) {  // shared tail page: copy on write
+      const int32_t p = page_alloc(c);
+      if (p < 0) return fail(c, QC_ERR_OOM, "KV page pool exhausted (%d pages)", c->cfg.max_pages);
+      if (!c->host_only) page_copy_jobs(c, q.pages[pi], p, cow);
+      page_decref(c, q.pages[pi]);
+      q.pages[pi] = p;
+      set_row(c, seq_ids[i]);
+    }
+  }
+  c->b_seq.assign(seq_ids, seq_ids + n);
+  c->b_pos.resize(n);
+  c->b_seg.assign(n + 1, 0);
+  for (int32_t i = 0; i < n; ++i) {
+    const Seq& q = c->seqs[seq_ids[i]];
+    c->b_pos[i] = q.len;
+    c->b_seg[i + 1] = c->b_seg[i] + 4 * (q.len / PAGE + 1);
+  }
+  c->b_has_tok = tokens != nullptr;
+  if (tokens) c->b_tok.assign(tokens, tokens + n);
+  c->b_total = c->b_seg[n];
+  c->b_grid = std::min(c->b_total, c->nsm);
+  c->b_per = (c->b_total + c->b_grid - 1) / c->b_grid;
+  c->b_grid = (c->b_total + c->b_per - 1) / c->b_per;
+  if (!c->host_only) {
+    int rc = run_jobs(c, cow, st, nullptr);
+    if (rc) return rc;
+    if ((rc = sync_rows(c, st))) return rc;
+    const size_t words = 5 * (size_t)n + 1;
+    char* buf = nullptr;
+    int si = 0;
+    if ((rc = stage_acquire(c, words * 4, &buf, &si))) return rc;
+    int32_t* d = reinterpret_cast<int32_t*>(buf);
+    // layout: slots[n] | pos[n] | seg[n+1] | page0[n] | append[n]
+    for (int32_t i = 0; i < n; ++i) {
+      d[i] = seq_ids[i];
+      d[n + i] = c->b_pos[i];
+      d[3 * n + 1 + i] = 0;
+      d[4 * n + 1 + i] = 1;
+    }
+    for (int32_t i = 0; i <= n; ++i) d[2 * n + i] = c->b_seg[i];
+    QC_CUDA(c, cudaMemcpyAsync(c->desc, buf, words * 4, cudaMemcpyHostToDevice, st));
+    if ((rc = stage_release(c, si, st))) return rc;
+  }
+  c->in_step = true;
+  return QC_OK;
+}
+
+int qc_attn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc_stream stream) {
+  if (!c || !proj || !out) return QC_ERR_ARG;
+  if (!c->in_step) return fail(c, QC_ERR_ARG, "no open decode step");
+  if (layer < 0 || layer >= c->cfg.n_attn_layers) return fail(c, QC_ERR_ARG, "attn layer %d", layer);
+  QC_NEED_DEVICE(c);
+  const int32_t n = (int32_t)c->b_seq.size();
+  const int64_t base = (int64_t)layer * c->cfg.max_pages * PAGE_ELEMS;
+  qc::AttnArgs a{};
+  a.proj = proj;
+  a.k_pool = c->k_pool + base;
+  a.v_pool = c->v_pool + base;
+  a.page_table = c->page_table;
+  a.pt_stride = c->pt_stride;
+  a.max_pages = c->cfg.max_pages;
+  a.slots = c->desc;
+  a.pos = c->desc + n;
+  a.seg = c->desc + 2 * n;
+  a.page0 = c->desc + 3 * n + 1;
+  a.append = c->desc + 4 * n + 1;
+  a.q_norm = c->q_norm + layer * HD;
+  a.k_norm = c->k_norm + layer * HD;
+  a.rope_cos = c->rope_cos;
+  a.rope_sin = c->rope_sin;
+  a.part_m = c->part_m;
+  a.part_l = c->part_l;
+  a.part_o = c->part_o;
+  a.n = n;
+  a.total = c->b_total;
+  a.per = c->b_per;
+  a.grid = c->b_grid;
+  a.err = c->dev_err;
+  qc::CombineArgs cb{};
+  cb.proj = proj;
+  cb.out = out;
+  cb.seg = a.seg;
+  cb.part_m = c->part_m;
+  cb.part_l = c->part_l;
+  cb.part_o = c->part_o;
+  cb.n = n;
+  cb.per = c->b_per;
+  QC_CUDA(c, qc::launch_attn_decode(a, cb, (cudaStream_t)stream));
+  return QC_OK;
+}
+
+int qc_gdn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc_stream stream) {
+  if (!c || !proj || !out) return QC_ERR_ARG;
+  if (!c->in_step) return fail(c, QC_ERR_ARG, "no open decode step");
+  if (layer < 0 || layer >= c->cfg.n_gdn_layers) return fail(c, QC_ERR_ARG, "gdn layer %d", layer);
+  QC_NEED_DEVICE(c);
+  const int32_t n = (int32_t)c->b_seq.size();
+  qc::GdnArgs g{};
+  g.proj = proj;
+  g.out = out;
+  g.state = slot_state(c, 0, layer);
+  g.ring = slot_ring(c, 0, layer);
+  g.state_stride = (int64_t)c->cfg.n_gdn_layers * QC_GDN_STATE;
+  g.ring_stride = (int64_t)c->cfg.n_gdn_layers * RING_ELEMS;
+  g.conv_w = c->conv_w + (int64_t)layer * 4 * QC_CONV_CH;
+  g.ssm_a = c->ssm_a + layer * 32;
+  g.dt_bias = c->dt_bias + layer * 32;
+  g.ssm_norm = c->ssm_norm + layer * 128;
+  g.slots = c->desc;
+  g.pos = c->desc + n;
+  g.n = n;
+  g.err = c->dev_err;
+  QC_CUDA(c, qc::launch_gdn_decode(g, (cudaStream_t)stream));
+  return QC_OK;
+}
+
+int qc_decode_end(qc_ctx* c) {
+  if (!c) return QC_ERR_ARG;
+  if (!c->in_step) return fail(c, QC_ERR_ARG, "no open decode step");
+  for (size_t i = 0; i < c->b_seq.size(); ++i) {
+    Seq& q = c->seqs[c->b_seq[i]];
+    if (c->b_has_tok && q.tokens.size() == (size_t)q.len) q.tokens.push_back(c->b_tok[i]);
+    q.len += 1;
+  }
+  c->in_step = false;
+  return QC_OK;
+}
+
+// ------------------------------------------------------------- prefix cache
+
+int qc_seq_match_prefix(qc_ctx* c, int32_t s, const int32_t* tokens, int32_t n,
+                        int32_t* prefix_len, qc_stream stream) {
+  if (!c || (!tokens && n > 0) || !prefix_len) return QC_ERR_ARG;
+  if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
+  const Seq& q = c->seqs[s];
+  // An unknown history (state stood up without tokens) never matches.
+  const bool known = q.tokens.size() == (size_t)q.len;
+  const int32_t cache_len = q.len;
+  int32_t prefix = 0;
+  if (known) {
+    const int32_t check = std::min(cache_len, n);
+    while (prefix < check && tokens[prefix] == q.tokens[prefix]) ++prefix;
+  }
+  if (prefix < cache_len || prefix >= n) {  // diverged, or nothing left to prefill
+    const bool empty = cache_len == 0;
+    prefix = 0;
+    if (!empty) {
+      int rc = qc_seq_reset(c, s, stream);
+      if (rc) return rc;
+    }
+  }
+  *prefix_len = prefix;
+  return QC_OK;
+}
+
+int qc_prefix_page_hashes(const int32_t* tokens, int32_t n, uint64_t* hashes) {
+  if ((!tokens && n > 0) || !hashes || n < 0) return QC_ERR_ARG;
+  uint64_t h = HASH_SEED;
+  for (int32_t i = 0; i < n / PAGE; ++i) {
+    h = page_hash(h, tokens + (int64_t)i * PAGE);
+    hashes[i] = h;
+  }
+  return QC_OK;
+}
+
+int qc_prefix_insert(qc_ctx* c, int32_t s, const int32_t* tokens, int32_t n, int32_t* entry,
+                     qc_stream stream) {
+  if (!c || !tokens || !entry || n <= 0) return QC_ERR_ARG;
+  if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
+  if (c->in_step) return fail(c, QC_ERR_ARG, "insert inside a decode step");
+  Seq& q = c->seqs[s];
+  if (q.len != n) return fail(c, QC_ERR_ARG, "sequence length %d != %d tokens", q.len, n);
+  if (q.tokens.size() == (size_t)n && !std::equal(tokens, tokens + n, q.tokens.begin()))
+    return fail(c, QC_ERR_ARG, "tokens differ from the sequence history");
+  if (c->free_snaps.empty()) return fail(c, QC_ERR_OOM, "no free snapshot slot");
+  const int32_t full = n / PAGE;
+  int32_t tail = -1;
+  if (n % PAGE) {
+    tail = page_alloc(c);
+    if (tail < 0) return fail(c, QC_ERR_OOM, "KV page pool exhausted (%d pages)", c->cfg.max_pages);
+  }
+  Entry e;
+  e.live = true;
+  e.P = n;
+  e.tokens.assign(tokens, tokens + n);
+  for (int32_t i = 0; i < full; ++i) {
+    e.pages.push_back(q.pages[i]);
+    c->page_ref[q.pages[i]] += 1;
+  }
+  if (tail >= 0) e.pages.push_back(tail);
+  e.snap = c->free_snaps.back();
+  c->free_snaps.pop_back();
+  uint64_t h = HASH_SEED;
+  for (int32_t i = 0; i < full; ++i) h = page_hash(h, tokens + (int64_t)i * PAGE);
+  e.key = h;
+  if (!c->host_only) {
+    std::vector<CopyJob> jobs;
+    const int ng = c->cfg.n_gdn_layers;
+    if (ng > 0) {
+      jobs.push_back({slot_state(c, s, 0), snap_state_ptr(c, e.snap), (int64_t)ng * QC_GDN_STATE * 4});
+      for (int l = 0; l < ng; ++l)
+        for (int j = 0; j < 3; ++j)
+          jobs.push_back({slot_ring(c, s, l) + (int64_t)((n - 3 + j) & 3) * QC_CONV_CH,
+                          snap_hist_ptr(c, e.snap, l) + (int64_t)j * QC_CONV_CH,
+                          (int64_t)QC_CONV_CH * 2});
+    }
+    if (tail >= 0) page_copy_jobs(c, q.pages[full], tail, jobs);
+    int rc = run_jobs(c, jobs, (cudaStream_t)stream, nullptr);
+    if (rc) return rc;
+  }
+  int32_t id = -1;
+  for (int32_t i = 0; i < (int32_t)c->entries.size(); ++i)
+    if (!c->entries[i].live) { id = i; break; }
+  if (id < 0) {
+    id = (int32_t)c->entries.size();
+    c->entries.emplace_back();
+  }
+  c->index[e.key].push_back(id);
+  c->entries[id] = std::move(e);
+  *entry = id;
+  return QC_OK;
+}
+
+int qc_prefix_lookup(qc_ctx* c, const int32_t* tokens, int32_t n, int32_t* matched,
+                     int32_t* entry) {
+  if (!c || (!tokens && n > 0) || !matched || !entry) return QC_ERR_ARG;
+  *matched = 0;
+  *entry = -1;
+  if (n <= 1) return QC_OK;
+  const int32_t m = n / PAGE;
+  std::vector<uint64_t> h(m + 1);
+  h[0] = HASH_SEED;
+  for (int32_t i = 0; i < m; ++i) h[i + 1] = page_hash(h[i], tokens + (int64_t)i * PAGE);
+  for (int32_t j = m; j >= 0; --j) {
+    auto it = c->index.find(h[j]);
+    if (it == c->index.end()) continue;
+    int32_t best = -1, best_p = 0;
+    for (int32_t id : it->second) {
+      const Entry& e = c->entries[id];
+      if (!e.live || e.P / PAGE != j || e.P >= n || e.P <= best_p) continue;
+      if (!std::equal(e.tokens.begin(), e.tokens.end(), tokens)) continue;  // verify ids
+      best = id;
+      best_p = e.P;
+    }
+    if (best >= 0) {
+      *matched = best_p;
+      *entry = best;
+      return QC_OK;
+    }
+  }
+  return QC_OK;
+}
+
+int qc_prefix_restore(qc_ctx* c, const int32_t* entries, const int32_t* seqs, int32_t n,
+                      qc_stream stream) {
+  if (!c || !entries || !seqs || n < 0) return QC_ERR_ARG;
+  if (c->in_step) return fail(c, QC_ERR_ARG, "restore inside a decode step");
+  for (int32_t i = 0; i < n; ++i) {
+    if (entries[i] < 0 || entries[i] >= (int32_t)c->entries.size() || !c->entries[entries[i]].live)
+      return fail(c, QC_ERR_ARG, "entry %d is not live", entries[i]);
+    if (!valid_seq(c, seqs[i])) return fail(c, QC_ERR_ARG, "sequence %d is not live", seqs[i]);
+    if (c->seqs[seqs[i]].len != 0 || !c->seqs[seqs[i]].pages.empty())
+      return fail(c, QC_ERR_ARG, "sequence %d is not empty (reset it first)", seqs[i]);
+    for (int32_t k = 0; k < i; ++k)
+      if (seqs[k] == seqs[i]) return fail(c, QC_ERR_ARG, "sequence %d restored twice", seqs[i]);
+  }
+  int32_t tails = 0;
+  for (int32_t i = 0; i < n; ++i) tails += (c->entries[entries[i]].P % PAGE) ? 1 : 0;
+  if (tails > (int32_t)c->free_pages.size())
+    return fail(c, QC_ERR_OOM, "KV page pool exhausted (%d pages)", c->cfg.max_pages);
+  std::vector<CopyJob> jobs;
+  const int ng = c->cfg.n_gdn_layers;
+  for (int32_t i = 0; i < n; ++i) {
+    const Entry& e = c->entries[entries[i]];
+    Seq& q = c->seqs[seqs[i]];
+    const int32_t full = e.P / PAGE;
+    for (int32_t k = 0; k < full; ++k) {  // page-list gather: share the full pages
+      q.pages.push_back(e.pages[k]);
+      c->page_ref[e.pages[k]] += 1;
+    }
+    if (e.P % PAGE) {  // tail page: copy on write
+      const int32_t p = page_alloc(c);
+      if (!c->host_only) page_copy_jobs(c, e.pages[full], p, jobs);
+      q.pages.push_back(p);
+    }
+    q.len = e.P;
+    q.tokens = e.tokens;
+    set_row(c, seqs[i]);
+    if (!c->host_only && ng > 0) {
+      jobs.push_back({snap_state_ptr(c, e.snap), slot_state(c, seqs[i], 0),
+                      (int64_t)ng * QC_GDN_STATE * 4});
+      for (int l = 0; l < ng; ++l)
+        for (int j = 0; j < 3; ++j)
+          jobs.push_back({snap_hist_ptr(c, e.snap, l) + (int64_t)j * QC_CONV_CH,
+                          slot_ring(c, seqs[i], l) + (int64_t)((e.P - 3 + j) & 3) * QC_CONV_CH,
+                          (int64_t)QC_CONV_CH * 2});
+    }
+  }
+  c->last_restore_bytes = 0;
+  if (!c->host_only) {
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = run_jobs(c, jobs, st, &c->last_restore_bytes);
+    if (rc) return rc;
+    if ((rc = sync_rows(c, st))) return rc;
+    // the page-table rows are part of the restore traffic
+    c->last_restore_bytes += 2LL * n * c->pt_stride * 4;
+  }
+  return QC_OK;
+}
+
+int qc_prefix_release(qc_ctx* c, int32_t id) {
+  if (!c) return QC_ERR_ARG;
+  if (id < 0 || id >= (int32_t)c->entries.size() || !c->entries[id].live)
+    return fail(c, QC_ERR_ARG, "entry %d is not live", id);
+  Entry& e = c->entries[id];
+  for (int32_t p : e.pages) page_decref(c, p);
+  auto& v = c->index[e.key];
+  v.erase(std::remove(v.begin(), v.end(), id), v.end());
+  if (v.empty()) c->index.erase(e.key);
+  c->free_snaps.push_back(e.snap);
+  e = Entry();
+  return QC_OK;
+}
+
+int qc_prefix_last_restore_bytes(const qc_ctx* c, int64_t* bytes) {
+  if (!c || !bytes) return QC_ERR_ARG;
+  *bytes = c->last_restore_bytes;
+  return QC_OK;
+}
+
+// ------------------------------------------------- split-K across devices
+
+int qc_attn_partial(qc_ctx* c, int layer, const uint16_t* proj, int32_t page_begin,
+                    int32_t page_end, int32_t append, float* partial, qc_stream stream) {
+  (void)layer; (void)proj; (void)page_begin; (void)page_end; (void)append; (void)partial;
+  (void)stream;
+  return fail(c, QC_ERR_ARG, "qc_attn_partial: not built yet");
+}
+
+int qc_attn_combine(qc_ctx* c, const float* partials, int32_t n_parts, const uint16_t* proj,
+                    uint16_t* out, qc_stream stream) {
+  (void)partials; (void)n_parts; (void)proj; (void)out; (void)stream;
+  return fail(c, QC_ERR_ARG, "qc_attn_combine: not built yet");
+}
+
+}  // extern "C"
