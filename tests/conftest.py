@@ -49,3 +49,11 @@ def oracle():
     ensure_built()
     import oracle as o
     return o
+
+
+@pytest.fixture(autouse=True)
+def _release_device_temporaries():
+    yield
+    mod = sys.modules.get("gpu_util")
+    if mod is not None:
+        mod.KEEP.clear()

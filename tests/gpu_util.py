@@ -8,11 +8,17 @@ OUT_ATOL, OUT_RTOL = 2e-2, 1e-2
 STATE_RTOL = 1e-4
 
 
+# Device copies made by dev() stay referenced until the test ends, so that a
+# pointer taken from a temporary (dev(x).data_ptr()) stays valid while the
+# asynchronous kernels that read it run.
+KEEP = []
+
+
 def dev(a: np.ndarray) -> torch.Tensor:
     a = np.ascontiguousarray(a)
-    if a.dtype == np.uint16:
-        return torch.from_numpy(a.view(np.int16)).cuda()
-    return torch.from_numpy(a).cuda()
+    t = torch.from_numpy(a.view(np.int16) if a.dtype == np.uint16 else a).cuda()
+    KEEP.append(t)
+    return t
 
 
 def host_u16(t: torch.Tensor) -> np.ndarray:

@@ -13,7 +13,7 @@ from gpu_util import (assert_out_close, assert_state_close, dev, empty_u16,  # n
 
 def make_ctx(qcache, n_seq, n_gdn=2):
     return qcache.QCache(n_attn_layers=1, n_gdn_layers=n_gdn, max_seqs=max(n_seq, 2),
-                         max_pages=8, max_ctx=1024, max_batch=max(n_seq, 2), max_snapshots=1,
+                         max_pages=2 * max(n_seq, 2), max_ctx=1024, max_batch=max(n_seq, 2), max_snapshots=1,
                          device=0)
 
 
