@@ -1,0 +1,436 @@
+"""Benchmark of the per-token cache path (BASELINE metric: decode cache-path
+µs/token/layer and HBM GB/s against 8 TB/s).
+
+Default workload (config 2 of the baseline): the full 32-layer hybrid cache
+stack (24 Gated-DeltaNet + 8 full-attention layers, attention at every 4th
+layer), 64 sequences at context 4096 in a paged bf16 KV cache (64-token pages,
+seeded random physical page order), one decode token per sequence per step,
+sequences sharded over the GPUs (no collective).  Synthetic seeded inputs;
+random-init per-layer weights of the real shapes.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  torchrun --nproc-per-node N bench.py --gpus N ...
+
+One JSON line on rank 0.  `value` = max-over-ranks device time of one step /
+(64 tokens x 32 layers), in µs.  `e2e` = the same metric through the C ABI
+with the step's projection inputs copied host->device from pinned memory and
+all outputs copied back inside the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "qwen3.5-9b-bfp8b-1xn300_b200")
+
+N_SEQ, CTX, N_LAYERS = 64, 4096, 32
+N_ATTN, N_GDN = 8, 24
+HBM_NOMINAL_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+# algorithmic bytes (HBM roofline; arithmetic intensity << ridge)
+GDN_BYTES_PER_SEQ = (2 * 32 * 128 * 128 * 4      # state read + write
+                     + 3 * 8192 * 2 + 8192 * 2   # conv ring: 3 taps read, 1 row written (bf16)
+                     + 12352 * 2 + 4096 * 2)     # projection row in, output out
+GDN_BYTES_PER_LAUNCH = 4 * 8192 * 4 + 32 * 4 * 2 + 128 * 4   # conv weights + small params
+
+
+def attn_bytes_per_seq(pos: int) -> int:
+    # K and V of the pos cached positions, the appended row, proj in, out
+    return 4096 * pos + 4096 + 10240 * 2 + 4096 * 2
+
+
+def is_attn(layer: int) -> bool:
+    return (layer + 1) % 4 == 0   # src/model_config.h:36-38
+
+
+def load_pkg(name):
+    full = "qcache_b200_" + name
+    if full in sys.modules:
+        return sys.modules[full]
+    spec = importlib.util.spec_from_file_location(full, os.path.join(PKG, name + ".py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[full] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------- GPU workload
+
+
+class Stack:
+    """The 32-layer cache stack for this rank's n sequences on one GPU."""
+
+    def __init__(self, qc, synth, torch, n, ctx, extra_tokens, seed, stream):
+        self.torch, self.n, self.ctx = torch, n, ctx
+        self.stream = stream
+        pages_per_seq = (ctx + extra_tokens) // 64 + 1
+        self.q = qc.QCache(n_attn_layers=N_ATTN, n_gdn_layers=N_GDN, max_seqs=n,
+                           max_pages=n * pages_per_seq, max_ctx=ctx + extra_tokens + 64,
+                           max_batch=n, max_snapshots=1, device=torch.cuda.current_device())
+        q = self.q
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed)
+        for l in range(N_ATTN):
+            a = synth.attn_inputs(seed + l, 1, 0)
+            q.set_attn_params(l, a["q_norm"], a["k_norm"])
+        for l in range(N_GDN):
+            p = synth.gdn_params(seed + 100 + l)
+            q.set_gdn_params(l, p["ssm_a"], p["dt_bias"], p["ssm_norm"], p["conv_w"])
+        self.seqs = [q.seq_alloc() for _ in range(n)]
+        # map pages in a seeded random order: physical pages end up permuted
+        rng = np.random.default_rng(seed)
+        need = {s: (ctx + 63) // 64 for s in self.seqs}
+        have = {s: 0 for s in self.seqs}
+        while any(have[s] < need[s] for s in self.seqs):
+            s = int(rng.choice([s for s in self.seqs if have[s] < need[s]]))
+            have[s] += 1
+            q.seq_reserve(s, min(ctx, have[s] * 64))
+        bf16 = torch.bfloat16
+        for s in self.seqs:
+            for l in range(N_ATTN):
+                k = torch.randn(ctx, 4, 256, generator=g, device="cuda").to(bf16)
+                v = torch.randn(ctx, 4, 256, generator=g, device="cuda").to(bf16)
+                q.kv_write(s, l, 0, ctx, k.data_ptr(), v.data_ptr(), stream)
+                torch.cuda.synchronize()
+            for l in range(N_GDN):
+                st = torch.randn(32, 128, 128, generator=g, device="cuda") * 0.02
+                hi = torch.randn(3, 8192, generator=g, device="cuda").to(bf16)
+                q.gdn_state_write(s, l, st.data_ptr(), hi.data_ptr(), stream)
+                torch.cuda.synchronize()
+        # per-layer projection inputs and outputs
+        self.proj = []
+        for layer in range(N_LAYERS):
+            w = 10240 if is_attn(layer) else 12352
+            self.proj.append(torch.randn(n, w, generator=g, device="cuda").to(bf16))
+        self.out = [torch.empty(n, 4096, device="cuda", dtype=bf16) for _ in range(N_LAYERS)]
+        torch.cuda.synchronize()
+        q.check_device()
+
+    def step(self, events=None):
+        q, st = self.q, self.stream
+        q.decode_begin(self.seqs, stream=st)
+        ai = gi = 0
+        for layer in range(N_LAYERS):
+            if events is not None:
+                events[layer][0].record()
+            if is_attn(layer):
+                q.attn_decode(ai, self.proj[layer].data_ptr(), self.out[layer].data_ptr(), st)
+                ai += 1
+            else:
+                q.gdn_decode(gi, self.proj[layer].data_ptr(), self.out[layer].data_ptr(), st)
+                gi += 1
+            if events is not None:
+                events[layer][1].record()
+        q.decode_end()
+
+    def step_bytes(self):
+        """Algorithmic HBM bytes of the next step (positions = current lengths)."""
+        pos = [self.q.seq_len(s) for s in self.seqs]
+        attn = sum(attn_bytes_per_seq(p) for p in pos)
+        gdn = self.n * GDN_BYTES_PER_SEQ + GDN_BYTES_PER_LAUNCH
+        return attn, gdn
+
+
+def run_ours(args, rank, world, dist):
+    import torch
+    qc = load_pkg("qcache")
+    synth = load_pkg("synth")
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    n = N_SEQ // world
+    stream = torch.cuda.current_stream().cuda_stream
+    stack = Stack(qc, synth, torch, n, CTX, args.warmup + args.steps + 8, seed=1000 + rank,
+                  stream=stream)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        stack.step()
+    barrier()
+
+    # ---- device-timed region: K steps, per-layer events for the roofline
+    attn_b = gdn_b = 0
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(N_LAYERS)]
+          for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    t0.record()
+    for k in range(args.steps):
+        a, g_ = stack.step_bytes()
+        attn_b += a
+        gdn_b += g_
+        stack.step(ev[k])
+    t1.record()
+    barrier()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    attn_ms = sum(ev[k][l][0].elapsed_time(ev[k][l][1]) for k in range(args.steps)
+                  for l in range(N_LAYERS) if is_attn(l)) / args.steps
+    gdn_ms = sum(ev[k][l][0].elapsed_time(ev[k][l][1]) for k in range(args.steps)
+                 for l in range(N_LAYERS) if not is_attn(l)) / args.steps
+    stack.q.check_device()
+
+    # ---- end-to-end through the C ABI with host buffers
+    bf16 = torch.bfloat16
+    h_in = [torch.empty(p.shape, dtype=bf16, pin_memory=True).copy_(p.cpu()) for p in stack.proj]
+    h_out = [torch.empty(o.shape, dtype=bf16, pin_memory=True) for o in stack.out]
+    h2d = sum(t.numel() * 2 for t in h_in)
+    d2h = sum(t.numel() * 2 for t in h_out)
+    e2e_steps = max(1, min(args.steps, 5))
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        for p, h in zip(stack.proj, h_in):
+            p.copy_(h, non_blocking=True)
+        stack.step()
+        for o, h in zip(stack.out, h_out):
+            h.copy_(o, non_blocking=True)
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+
+    vals = torch.tensor([ms, e2e_ms, attn_ms, gdn_ms], device="cuda", dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, attn_ms, gdn_ms = vals.tolist()
+    return dict(ms=ms, e2e_ms=e2e_ms, attn_ms=attn_ms, gdn_ms=gdn_ms,
+                attn_bytes=attn_b / args.steps, gdn_bytes=gdn_b / args.steps, n_local=n,
+                h2d=h2d, d2h=d2h, clocks=clk)
+
+
+# ------------------------------------------------------------ CPU baseline
+
+
+def cpu_baseline(budget_s: float = 12.0, threads: int | None = None):
+    """The oracle's threaded C++ restatement of the reference's host math
+    (liboracle_fast.so: the reference's -O3 -ffast-math), timed on this host
+    over a bounded sample of the same workload: sequences at context 4096, one
+    DeltaNet layer and one attention layer per sample, combined 24:8 per
+    token.  Returns µs per token per layer."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ctypes as C
+
+    import oracle
+
+    synth = load_pkg("synth")
+    L = oracle.lib(fast=True)
+    threads = threads or os.cpu_count() or 1
+    nb = max(1, min(threads, 16))              # sequences per batch call
+    p = synth.gdn_params(1)
+    g = synth.gdn_inputs(2, nb)
+    hist = np.ascontiguousarray(synth.bf16_to_f32(g["hist"]))
+    state = np.ascontiguousarray(g["state"])
+    out = np.zeros((nb, 4096), np.float32)
+    ptr = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
+    # attention: nb sequences sharing one seeded cache content (bounded memory)
+    a = synth.attn_inputs(3, 1, CTX)
+    cap = CTX + 64
+    kc = np.zeros((nb, cap, 4, 256), np.uint16)
+    vc = np.zeros((nb, cap, 4, 256), np.uint16)
+    kc[:, :CTX], vc[:, :CTX] = a["k"][0], a["v"][0]
+    aproj = np.ascontiguousarray(np.repeat(a["proj"], nb, axis=0))
+    pos = np.full(nb, CTX, np.int32)
+    aout = np.zeros((nb, 4096), np.float32)
+
+    def gdn_once():
+        L.qo_gdn_decode_batch(nb, ptr(g["proj"]), ptr(state), ptr(hist), ptr(p["conv_w"]),
+                              ptr(p["ssm_a"]), ptr(p["dt_bias"]), ptr(p["ssm_norm"]), ptr(out),
+                              0, threads)
+
+    def attn_once():
+        L.qo_attn_decode_batch(nb, ptr(aproj), ptr(a["q_norm"]), ptr(a["k_norm"]), ptr(pos),
+                               ptr(kc), ptr(vc), cap, ptr(aout), 0, threads)
+
+    def timed(fn, share):
+        fn()  # warm
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            fn()
+            reps += 1
+            el = time.perf_counter() - t0
+            if el > budget_s * share:
+                return el / (reps * nb), reps
+    t_gdn, r_g = timed(gdn_once, 0.4)
+    t_attn, r_a = timed(attn_once, 0.6)
+    us = (24 * t_gdn + 8 * t_attn) / 32 * 1e6
+    sample = (f"{r_g}x{nb} seq DeltaNet steps + {r_a}x{nb} seq attention steps at ctx {CTX}, "
+              f"weighted 24:8 per token")
+    return us, threads, sample, t_gdn * 1e6, t_attn * 1e6
+
+
+# ----------------------------------------------------------------- output
+
+
+def emit(line):
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    workload = (f"full cache stack: 24 DeltaNet + 8 attention layers, {N_SEQ} sequences at "
+                f"context {CTX}, 64-token bf16 pages (permuted), 1 decode token per sequence")
+    config = {"workload": workload, "sequences": N_SEQ, "context": CTX, "layers": N_LAYERS,
+              "page_tokens": 64, "sharding": f"sequences over {world} GPU(s), no collective",
+              "l2": "inputs larger than L2 (~15 GB of KV/state per step)"}
+    metric = "decode cache-path us/token/layer"
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        us, cores, sample, _, _ = cpu_baseline()
+        emit({"impl": "reference", "metric": metric, "value": round(us, 3), "unit": "us",
+              "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+              "higher_is_better": False, "dtype": "f32", "data": "synthetic", "config": config,
+              "cpu_baseline": {"value": round(us, 3), "unit": "us/token/layer", "cores": cores,
+                               "kind": "port", "sample": sample},
+              "e2e": {"value": round(us, 3), "unit": "us", "h2d_bytes_per_step": 0,
+                      "d2h_bytes_per_step": 0}})
+        return
+
+    dist = None
+    if world > 1:
+        import torch
+        import torch.distributed as dist_mod
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist_mod.init_process_group("nccl")
+        dist = dist_mod
+    r = run_ours(args, rank, world, dist)
+    if dist is not None:
+        dist.barrier()
+    if rank != 0:
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+    peak, peak_kind = measured_peaks()
+    units = N_SEQ * N_LAYERS
+    us = r["ms"] * 1e3 / units
+    step_bytes = (r["attn_bytes"] + r["gdn_bytes"]) * world
+    gbs = step_bytes / (r["ms"] * 1e-3) / 1e9
+    # dominant kernel: the layer type with the larger device time per step
+    if r["attn_ms"] >= r["gdn_ms"]:
+        kname, kbytes, kms = "attn_partial+combine (per attention layer)", r["attn_bytes"] / N_ATTN, r["attn_ms"] / N_ATTN
+    else:
+        kname, kbytes, kms = "gdn_decode (per DeltaNet layer)", r["gdn_bytes"] / N_GDN, r["gdn_ms"] / N_GDN
+    k_gbs = kbytes / (kms * 1e-3) / 1e9
+    line = {
+        "metric": metric, "value": round(us, 4), "unit": "us", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 4),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded), random-init per-layer weights", "config": config,
+        "hbm": {"algorithmic_bytes_per_step": int(step_bytes), "achieved_gbs": round(gbs, 1),
+                "frac_of_8tbs": round(gbs / world / HBM_NOMINAL_GBS, 4),
+                "frac_of_measured": round(gbs / world / peak, 4)},
+        "layer_time_ms": {"attention_8_layers": round(r["attn_ms"], 4),
+                          "deltanet_24_layers": round(r["gdn_ms"], 4)},
+        "roofline": {"kernel": kname, "bound": "hbm", "achieved": round(k_gbs, 1),
+                     "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": round(k_gbs / peak, 4), "traffic": None},
+        "e2e": {"value": round(r["e2e_ms"] * 1e3 / units, 4), "unit": "us",
+                "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+        "gpu_launches": args.steps * (N_GDN + 2 * N_ATTN),
+        "clocks": r["clocks"],
+    }
+    if not args.no_cpu_baseline and world == 1:
+        cus, cores, sample, _, _ = cpu_baseline()
+        line["cpu_baseline"] = {"value": round(cus, 3), "unit": "us/token/layer", "cores": cores,
+                                "kind": "port", "sample": sample}
+    emit(line)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
