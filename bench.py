@@ -92,7 +92,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -200,7 +200,8 @@ class Stack:
         q.decode_end()
 
     def step_bytes(self):
-        """Algorithmic HBM bytes of the next step (positions = current lengths)."""
+        """Algorithmic HBM bytes of ONE layer launch of each type in the next
+        step (positions = current lengths)."""
         pos = [self.q.seq_len(s) for s in self.seqs]
         attn = sum(attn_bytes_per_seq(p) for p in pos)
         gdn = self.n * GDN_BYTES_PER_SEQ + GDN_BYTES_PER_LAUNCH
@@ -213,7 +214,7 @@ def run_ours(args, rank, world, dist):
     synth = load_pkg("synth")
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    n = N_SEQ // world
+    n = args.seqs // world
     stream = torch.cuda.current_stream().cuda_stream
     stack = Stack(qc, synth, torch, n, CTX, args.warmup + args.steps + 8, seed=1000 + rank,
                   stream=stream)
@@ -233,6 +234,7 @@ def run_ours(args, rank, world, dist):
           for _ in range(args.steps)]
     clocks = ClockSampler(local)
     clocks.start()
+    time.sleep(0.5)   # let the sampler come up before the timed region
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     barrier()
@@ -278,7 +280,8 @@ def run_ours(args, rank, world, dist):
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     ms, e2e_ms, attn_ms, gdn_ms = vals.tolist()
     return dict(ms=ms, e2e_ms=e2e_ms, attn_ms=attn_ms, gdn_ms=gdn_ms,
-                attn_bytes=attn_b / args.steps, gdn_bytes=gdn_b / args.steps, n_local=n,
+                attn_layer_bytes=attn_b / args.steps, gdn_layer_bytes=gdn_b / args.steps,
+                n_local=n,
                 h2d=h2d, d2h=d2h, clocks=clk)
 
 
@@ -353,17 +356,20 @@ def emit(line):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--seqs", type=int, default=N_SEQ,
+                    help="total sequences (smaller values only for profiling captures)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    workload = (f"full cache stack: 24 DeltaNet + 8 attention layers, {N_SEQ} sequences at "
+    workload = (f"full cache stack: 24 DeltaNet + 8 attention layers, {args.seqs} sequences at "
                 f"context {CTX}, 64-token bf16 pages (permuted), 1 decode token per sequence")
-    config = {"workload": workload, "sequences": N_SEQ, "context": CTX, "layers": N_LAYERS,
-              "page_tokens": 64, "sharding": f"sequences over {world} GPU(s), no collective",
+    config = {"workload": workload, "sequences": args.seqs, "context": CTX, "layers": N_LAYERS,
+              "page_tokens": 64, "timing": "CUDA events on the launching stream, max over ranks",
+              "sharding": f"sequences over {world} GPU(s), no collective",
               "l2": "inputs larger than L2 (~15 GB of KV/state per step)"}
     metric = "decode cache-path us/token/layer"
 
@@ -395,15 +401,19 @@ def main():
             dist.destroy_process_group()
         return
     peak, peak_kind = measured_peaks()
-    units = N_SEQ * N_LAYERS
+    units = args.seqs * N_LAYERS
     us = r["ms"] * 1e3 / units
-    step_bytes = (r["attn_bytes"] + r["gdn_bytes"]) * world
+    # every rank holds the same number of sequences at the same context
+    step_bytes = (N_ATTN * r["attn_layer_bytes"] + N_GDN * r["gdn_layer_bytes"]) * world
     gbs = step_bytes / (r["ms"] * 1e-3) / 1e9
-    # dominant kernel: the layer type with the larger device time per step
+    # dominant kernel: the layer type with the larger device time per step;
+    # achieved = its algorithmic bytes per launch / its average launch time
     if r["attn_ms"] >= r["gdn_ms"]:
-        kname, kbytes, kms = "attn_partial+combine (per attention layer)", r["attn_bytes"] / N_ATTN, r["attn_ms"] / N_ATTN
+        kname, kbytes, kms = ("attn_partial_kernel + attn_combine_kernel (one attention layer)",
+                              r["attn_layer_bytes"], r["attn_ms"] / N_ATTN)
     else:
-        kname, kbytes, kms = "gdn_decode (per DeltaNet layer)", r["gdn_bytes"] / N_GDN, r["gdn_ms"] / N_GDN
+        kname, kbytes, kms = ("gdn_decode_kernel (one DeltaNet layer)", r["gdn_layer_bytes"],
+                              r["gdn_ms"] / N_GDN)
     k_gbs = kbytes / (kms * 1e-3) / 1e9
     line = {
         "metric": metric, "value": round(us, 4), "unit": "us", "n_gpus": world,
