@@ -1,9 +1,11 @@
 // gdn_decode.cu — one Gated-DeltaNet decode step, fused in a single
 // memory-bound pass (src/engine.cpp:3204-3327).
 //
-// Work split: a cluster of R CTAs per (sequence, v-head); CTA r of the cluster
-// owns state rows [r*128/R, (r+1)*128/R) of that head (rows are independent in
-// the delta rule, src/engine.cpp:3284-3305).  The CTA
+// Work split: R CTAs per (sequence, v-head) — R = 1 (one 256-thread CTA per
+// head) for large batches, a cluster of R = 8 for batches of at most 8, which
+// would otherwise leave most of the 148 SMs idle.  CTA r owns state rows
+// [r*128/R, (r+1)*128/R) of the head (rows are independent in the delta rule,
+// src/engine.cpp:3284-3305).  The CTA
 //   1. starts one bulk copy (TMA, cp.async.bulk) of its 128/R x 512 B state
 //      slice into shared memory;
 //   2. meanwhile runs the causal conv (width 4) + SiLU for the 128 q and 128 k
@@ -13,9 +15,9 @@
 //   4. per row: decay, s·k, delta, rank-1 update, s·q — one float4 per lane,
 //      warp-shuffle dot products — and stores the row straight back to HBM
 //      with 128-bit stores;
-//   5. gated RMSNorm over the head's 128 outputs: the CTAs of the cluster
-//      exchange their partial sums of squares through distributed shared
-//      memory (no multicast), then each CTA writes its outputs as bf16.
+//   5. gated RMSNorm over the head's 128 outputs (for R > 1 the CTAs of the
+//      cluster exchange their partial sums of squares through distributed
+//      shared memory, plain stores, no multicast), then bf16 outputs.
 // HBM traffic per (sequence, layer): state 2 MiB read + 2 MiB written, conv
 // ring 3 x 16 KiB read + 16 KiB written, projection row 24.7 KB, output 8 KB.
 //
@@ -43,26 +45,28 @@ constexpr int B_OFF = 12320;         // beta offset
 constexpr float EPS = 1e-6f;
 constexpr float SSM_SCALE = 1.0f / 11.3137f;  // src/engine.cpp:3249
 
-template <int R>
-__global__ void __launch_bounds__(128) gdn_decode_kernel(const GdnArgs a) {
-  constexpr int RB = HK / R;   // state rows per CTA
-  constexpr int RPW = RB / 4;  // rows per warp
-  __shared__ __align__(128) float s_state[RB * HK];
+// R CTAs (a cluster when R > 1) per (sequence, v-head), T threads each.
+template <int R, int T>
+__global__ void __launch_bounds__(T) gdn_decode_kernel(const GdnArgs a) {
+  constexpr int RB = HK / R;     // state rows per CTA
+  constexpr int NW = T / 32;     // warps
+  constexpr int RPW = RB / NW;   // rows per warp
+  static_assert(RPW >= 1 && RPW <= 32 && RB % NW == 0, "row split");
+  extern __shared__ __align__(128) float s_state[];  // [RB][128]
   __shared__ __align__(16) float s_q[HK];
   __shared__ __align__(16) float s_k[HK];
   __shared__ float s_v[RB];
   __shared__ float s_z[RB];
   __shared__ float s_o[RB];
-  __shared__ float s_red[8];
-  __shared__ float s_ssq;
+  __shared__ float s_red[2 * NW];
+  __shared__ float s_ssq[R];
   __shared__ __align__(8) uint64_t s_bar;
 
-  cg::cluster_group cluster = cg::this_cluster();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = blockIdx.y;
   const int vh = blockIdx.x / R;
-  const int r = static_cast<int>(cluster.block_rank());
-  const int kh = vh & 15;  // kh = vh % 16 (src/engine.cpp:3254)
+  const int r = blockIdx.x % R;  // == rank in the cluster (cluster dims (R,1,1))
+  const int kh = vh & 15;        // kh = vh % 16 (src/engine.cpp:3254)
   const int slot = a.slots[b];
   const int pos = a.pos[b];
   float* st = a.state + slot * a.state_stride + (int64_t)vh * HK * HK + (int64_t)r * RB * HK;
@@ -78,6 +82,10 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const GdnArgs a) {
     mbar_arrive_expect_tx(&s_bar, RB * HK * 4);
     bulk_g2s(s_state, st, RB * HK * 4, &s_bar);
   }
+  // Split cluster barrier, first half: announces that this CTA runs, so that
+  // peers may write its shared memory after their matching wait.  Relaxed:
+  // no memory ordering is needed here, and its latency hides behind the conv.
+  if constexpr (R > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
   // ---- conv1d + SiLU (src/engine.cpp:3204-3234), ring append
   const int t0 = (pos - 3) & 3, t1 = (pos - 2) & 3, t2 = (pos - 1) & 3, tw = pos & 3;
@@ -89,52 +97,57 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const GdnArgs a) {
     y = fmaf(bf2f(x[c]), w[3 * CONV + c], y);
     return silu_exact(y);
   };
-  const int cq = kh * HK + tid;
-  const int ck = 2048 + kh * HK + tid;
-  const float qv = conv1(cq);
-  const float kv = conv1(ck);
-  if (vh < 16 && tid / RB == r) {  // one CTA of one v-head writes each q/k channel
-    ring[tw * CONV + cq] = x[cq];
-    ring[tw * CONV + ck] = x[ck];
+  // q channels kh*128 + i and k channels 2048 + kh*128 + i, i < 128
+  float sq = 0.0f, sk = 0.0f;
+  for (int i = tid; i < 2 * HK; i += T) {
+    const int c = (i < HK) ? kh * HK + i : 2048 + kh * HK + (i - HK);
+    const float y = conv1(c);
+    if (i < HK) { s_q[i] = y; sq = fmaf(y, y, sq); }
+    else { s_k[i - HK] = y; sk = fmaf(y, y, sk); }
+    // one CTA of one v-head writes each q/k channel of the ring
+    if (vh < 16 && (i & (HK - 1)) / RB == r) ring[tw * CONV + c] = x[c];
   }
-  if (tid < RB) {
-    const int cv = 4096 + vh * HK + r * RB + tid;
-    s_v[tid] = conv1(cv);
+  for (int i = tid; i < RB; i += T) {
+    const int cv = 4096 + vh * HK + r * RB + i;
+    s_v[i] = conv1(cv);
     ring[tw * CONV + cv] = x[cv];
-    s_z[tid] = bf2f(x[Z_OFF + vh * HK + r * RB + tid]);
+    s_z[i] = bf2f(x[Z_OFF + vh * HK + r * RB + i]);
   }
 
   // ---- L2 normalisation of q and k (src/engine.cpp:3261-3275)
-  {
-    const float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv);
-    if (lane == 0) {
-      s_red[warp] = sq;
-      s_red[4 + warp] = sk;
-    }
-    __syncthreads();
-    const float tq = (s_red[0] + s_red[1]) + (s_red[2] + s_red[3]);
-    const float tk = (s_red[4] + s_red[5]) + (s_red[6] + s_red[7]);
-    s_q[tid] = qv * (1.0f / sqrtf(tq + EPS));
-    s_k[tid] = kv * (1.0f / sqrtf(tk + EPS));
+  sq = warp_sum(sq);
+  sk = warp_sum(sk);
+  if (lane == 0) {
+    s_red[warp] = sq;
+    s_red[NW + warp] = sk;
   }
+  __syncthreads();
+  float tq = 0.0f, tk = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NW; ++i) {
+    tq += s_red[i];
+    tk += s_red[NW + i];
+  }
+  const float qs = 1.0f / sqrtf(tq + EPS), ks = 1.0f / sqrtf(tk + EPS);
 
   // ---- decay and beta (src/engine.cpp:3277-3281)
   const float biased = bf2f(x[A_OFF + vh]) + a.dt_bias[vh];
   const float sp = (biased > 20.0f) ? biased : logf(1.0f + expf(biased));
   const float decay = expf(sp * a.ssm_a[vh]);
   const float beta = sigmoid_exact(bf2f(x[B_OFF + vh]));
-  __syncthreads();  // s_q, s_k, s_v ready
 
-  const bool ok = mbar_wait(&s_bar, 0, a.err);
+  const bool ok = __syncthreads_and(mbar_wait(&s_bar, 0, a.err));
 
   // ---- delta rule (src/engine.cpp:3284-3305), rows of this warp
   float ssq_w = 0.0f;
   if (ok) {
-    const float4 k4 = reinterpret_cast<const float4*>(s_k)[lane];
-    const float4 q4 = reinterpret_cast<const float4*>(s_q)[lane];
+    float4 k4 = reinterpret_cast<const float4*>(s_k)[lane];
+    float4 q4 = reinterpret_cast<const float4*>(s_q)[lane];
+    k4.x *= ks; k4.y *= ks; k4.z *= ks; k4.w *= ks;
+    q4.x *= qs; q4.y *= qs; q4.z *= qs; q4.w *= qs;
     const float4* srow = reinterpret_cast<const float4*>(s_state);
     float4 rr[RPW];
-    float sk[RPW];
+    float skr[RPW];
 #pragma unroll
     for (int i = 0; i < RPW; ++i) {
       float4 v = srow[(warp * RPW + i) * 32 + lane];
@@ -144,24 +157,24 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const GdnArgs a) {
       d = fmaf(v.y, k4.y, d);
       d = fmaf(v.z, k4.z, d);
       d = fmaf(v.w, k4.w, d);
-      sk[i] = d;
+      skr[i] = d;
     }
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1)
 #pragma unroll
-      for (int i = 0; i < RPW; ++i) sk[i] += __shfl_xor_sync(FULL_MASK, sk[i], m);
+      for (int i = 0; i < RPW; ++i) skr[i] += __shfl_xor_sync(FULL_MASK, skr[i], m);
     float o[RPW];
     float4* grow = reinterpret_cast<float4*>(st);
 #pragma unroll
     for (int i = 0; i < RPW; ++i) {
       const int row = warp * RPW + i;
-      const float dd = beta * (s_v[row] - sk[i]);
+      const float dd = beta * (s_v[row] - skr[i]);
       float4 v = rr[i];
       v.x = fmaf(k4.x, dd, v.x);
       v.y = fmaf(k4.y, dd, v.y);
       v.z = fmaf(k4.z, dd, v.z);
       v.w = fmaf(k4.w, dd, v.w);
-      grow[row * 32 + lane] = v;  // coalesced 512 B per row
+      __stcs(grow + row * 32 + lane, v);  // coalesced 512 B per row, streamed
       float d = v.x * q4.x;
       d = fmaf(v.y, q4.y, d);
       d = fmaf(v.z, q4.z, d);
@@ -179,31 +192,53 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const GdnArgs a) {
       ssq_w = fmaf(ov, ov, ssq_w);
     }
   }
+  __syncthreads();  // s_red reuse
   if (lane == 0) s_red[warp] = ssq_w;
   __syncthreads();
-  if (tid == 0) s_ssq = (s_red[0] + s_red[1]) + (s_red[2] + s_red[3]);
+  float part = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NW; ++i) part += s_red[i];
 
   // ---- gated RMSNorm over the head's 128 outputs (src/engine.cpp:3307-3322)
-  cluster.sync();
-  float tot = 0.0f;
+  float tot = part;
+  if constexpr (R > 1) {
+    // every CTA pushes its partial sum of squares into slot r of each peer's
+    // s_ssq (distributed shared memory, plain stores), then one cluster
+    // barrier (release/acquire) publishes them; nobody reads remote memory
+    // after the barrier, so CTAs may exit right after it
+    cg::cluster_group cluster = cg::this_cluster();
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every peer has started
+    if (tid < R) *cluster.map_shared_rank(&s_ssq[r], tid) = part;
+    cluster.sync();
+    tot = 0.0f;
 #pragma unroll
-  for (int q = 0; q < R; ++q) tot += *cluster.map_shared_rank(&s_ssq, q);
-  cluster.sync();  // peers may leave only after every CTA has read their sum
+    for (int q = 0; q < R; ++q) tot += s_ssq[q];
+  }
   if (!ok) return;
-  if (tid < RB) {
-    const float rms = 1.0f / sqrtf(tot / 128.0f + EPS);
-    const int d = r * RB + tid;
-    const float y = (s_o[tid] * rms) * a.ssm_norm[d] * silu_exact(s_z[tid]);
+  const float rms = 1.0f / sqrtf(tot / 128.0f + EPS);
+  for (int i = tid; i < RB; i += T) {
+    const int d = r * RB + i;
+    const float y = (s_o[i] * rms) * a.ssm_norm[d] * silu_exact(s_z[i]);
     a.out[(int64_t)b * 4096 + vh * HK + d] = f2bf(y);
   }
 }
 
-template <int R>
+template <int R, int T>
 cudaError_t launch_r(const GdnArgs& a, cudaStream_t s) {
+  constexpr int smem = (HK / R) * HK * 4;
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(gdn_decode_kernel<R, T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured_device = dev;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(32 * R, a.n, 1);
-  cfg.blockDim = dim3(128, 1, 1);
-  cfg.dynamicSmemBytes = 0;
+  cfg.blockDim = dim3(T, 1, 1);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -211,17 +246,19 @@ cudaError_t launch_r(const GdnArgs& a, cudaStream_t s) {
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<R>, a);
+  cfg.numAttrs = R > 1 ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<R, T>, a);
 }
 
 }  // namespace
 
 cudaError_t launch_gdn_decode(const GdnArgs& a, cudaStream_t s) {
   if (a.n <= 0) return cudaSuccess;
-  // Small batches split each head over more CTAs to fill the 148 SMs.
-  if (a.n <= 8) return launch_r<8>(a, s);
-  return launch_r<4>(a, s);
+  // Small batches split each head over a cluster of 8 CTAs to fill the 148
+  // SMs; large batches give each (sequence, head) one CTA streaming the whole
+  // 64 KiB state slice.
+  if (a.n <= 8) return launch_r<8, 128>(a, s);
+  return launch_r<1, 256>(a, s);
 }
 
 }  // namespace qc
