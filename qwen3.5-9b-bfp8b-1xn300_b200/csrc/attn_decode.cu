@@ -3,23 +3,30 @@
 //
 // Kernel 1, attn_partial_kernel: one CTA per SM, each given an equal share of
 // the batch's "page-heads" (one 64-token page of one kv-head: 32 KiB of K and
-// 32 KiB of V, contiguous in the pool) in (sequence, kv-head, page) order —
-// a split-K over KV positions that balances the work exactly whatever the
-// mix of context lengths.  Warp 8 is the producer: it streams each page-head
-// into a 2-stage shared-memory ring with two bulk copies (cp.async.bulk, the
-// untiled TMA path; no multicast).  Warps 0-7 are consumers; each takes 8 of
-// the 64 positions of a tile for all 4 query heads of the GQA group
-// (kv_h = h / 4, src/engine.cpp:3532), keeps its own online-softmax state
-// (m, l, o) in registers and reduces the 32 (position, head) dot products of
-// a tile with one transposing warp-shuffle reduction (31 shuffles).  When the
-// CTA leaves a (sequence, kv-head) pair it merges its 8 warps' states and
-// writes one partial record.
+// 32 KiB of V) in (sequence, kv-head, page) order — a split-K over KV
+// positions that balances the work exactly whatever the mix of context
+// lengths.  Warp 8 is the producer: it streams each page-head into a 3-stage
+// shared-memory ring with tiled TMA loads (cp.async.bulk.tensor, 16-row x
+// 128-byte boxes, 128-byte swizzle so that the ldmatrix reads below are free
+// of bank conflicts; each CTA loads only for itself).  Warps 0-7 are consumers; each takes 8 of
+// the 64 positions of a tile for the 4 query heads of the GQA group
+// (kv_h = h / 4, src/engine.cpp:3532) and keeps its own online-softmax state.
 //
-// Fused prologue per pair: per-head RMSNorm + partial RoPE of the 4 query
-// heads (src/engine.cpp:3497-3519) and, in the CTA that owns the page of the
-// new position, the same for the new K plus the bf16 append of K and V into
-// the page (src/engine.cpp:3521-3526); the new token is attended from shared
-// memory, so no CTA reads a row another CTA is writing.
+// The dot products run on the tensor cores (mma.sync, bf16 in, fp32
+// accumulate), operands straight from the swizzled tiles via ldmatrix:
+//   S^T[8 pos x 8 col] = K[8 pos x 256] . Qx^T, where the 8 columns hold the 4
+//     heads' q rounded to bf16 (hi) and the bf16 rounding residual (lo), so
+//     S = S_hi + S_lo carries ~16 mantissa bits of q;
+//   O^T[256 x 8 col] += V^T[256 x 8 pos] . Px^T with the same hi/lo split of
+//     the softmax weights, transposed from the S accumulators by movmatrix.
+// K and V are bf16 in the cache, so the products are exact and the result
+// matches an fp32 computation to ~1e-5 relative.
+//
+// Fused prologue per (sequence, kv-head) pair: per-head RMSNorm + partial RoPE
+// of the 4 query heads (src/engine.cpp:3497-3519) and, in the CTA that owns
+// the page of the new position, the same for the new K plus the bf16 append of
+// K and V into the page (src/engine.cpp:3521-3526); the new token is attended
+// from shared memory, so no CTA reads a row another CTA is writing.
 //
 // Kernel 2, attn_combine_kernel: per (sequence, kv-head) merges the partial
 // records of the CTAs that covered it, divides by the softmax sum and applies
@@ -34,22 +41,24 @@ namespace {
 
 constexpr int HD = 256;
 constexpr int PAGE = 64;
-constexpr int STAGES = 2;
+constexpr int STAGES = 3;
 constexpr int N_CONSUMER = 8;
 constexpr int THREADS = (N_CONSUMER + 1) * 32;
-constexpr int TILE_BYTES = PAGE * HD * 2;  // 32 KiB for K or for V
+constexpr int TILE_ELEMS = PAGE * HD;     // one K or V page-head, 32 KiB
+constexpr int BOX_ROWS = 16;              // TMA box: 16 rows x 64 bf16 (2 KiB)
+constexpr int BOX_BYTES = BOX_ROWS * 128;
 // score * 1/16 (src/model_config.h:40), kept in the log2 domain for exp2
 constexpr float SCALE_LOG2 = 0.0625f * 1.4426950408889634f;
 
-struct Smem {
-  uint16_t k[STAGES][PAGE * HD];
-  uint16_t v[STAGES][PAGE * HD];
-  float red_o[N_CONSUMER][4][HD];
+struct __align__(1024) Smem {
+  uint16_t k[STAGES][TILE_ELEMS];   // swizzled: [col block 4][row 64][128 B]
+  uint16_t v[STAGES][TILE_ELEMS];
+  float red_o[4][4][HD];            // flush: 4 warps at a time
   float q[4][HD];
   float red_ml[N_CONSUMER][8];
-  float p[N_CONSUMER][32];
   uint16_t knew[HD];
   uint16_t vnew[HD];
+  uint16_t zero[HD];
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
 };
@@ -58,20 +67,62 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(N_CONSUMER * 32) : "memory");
 }
 
-// lane l returns the sum over the warp of v[l] (a transposing reduction:
-// 16 + 8 + 4 + 2 + 1 shuffles for 32 independent sums).
-__device__ __forceinline__ float transpose_reduce32(float (&v)[32], int lane) {
-#pragma unroll
-  for (int k = 16; k >= 1; k >>= 1) {
-    const bool hi = (lane & k) != 0;
-#pragma unroll
-    for (int j = 0; j < k; ++j) {
-      const float send = hi ? v[j] : v[j + k];
-      const float keep = hi ? v[j + k] : v[j];
-      v[j] = keep + __shfl_xor_sync(FULL_MASK, send, k);
-    }
-  }
-  return v[0];
+// Byte offset of (row, dim) inside a swizzled 64 x 256 bf16 tile: four
+// 64-column blocks of 64 rows x 128 B; the 16-byte chunk index within a row is
+// XORed with row % 8 (the TMA 128-byte swizzle).
+__device__ __forceinline__ uint32_t swz(int row, int dim) {
+  return (uint32_t)((dim >> 6) * (PAGE * 128) + row * 128 + ((((dim & 63) >> 3) ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D += A[16x16] . B[16x8], bf16 in, f32 accumulate (rows 8..15 of A are zero)
+__device__ __forceinline__ void mma_k16(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+// D += A[16x8] . B[8x8]
+__device__ __forceinline__ void mma_k8(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
+  return uint32_t(f2bf(lo_elem)) | (uint32_t(f2bf(hi_elem)) << 16);
+}
+// split x into bf16 hi + bf16 lo (x - hi), as bit patterns
+__device__ __forceinline__ void split_bf16(float x, uint16_t& hi, uint16_t& lo) {
+  hi = f2bf(x);
+  lo = f2bf(x - bf2f(hi));
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 
 // Walks page-heads u in (sequence b, kv-head, page) order.
@@ -94,8 +145,7 @@ struct Cursor {
     pg = 0;
     if (++kvh < 4) return;
     kvh = 0;
-    // skip sequences with no pages in range
-    do {
+    do {  // skip sequences with no pages in range
       ++b;
       np = (b < a.n) ? ((a.seg[b + 1] - a.seg[b]) >> 2) : 1;
     } while (np == 0);
@@ -122,9 +172,12 @@ __device__ __forceinline__ TileInfo tile_info(const AttnArgs& a, const Cursor& c
   return t;
 }
 
-__global__ void __launch_bounds__(THREADS, 1) attn_partial_kernel(const AttnArgs a) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+__global__ void __launch_bounds__(THREADS, 1)
+    attn_partial_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv) {
+  extern __shared__ unsigned char smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                      ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int u_begin = blockIdx.x * a.per;
   const int u_end = min(a.total, u_begin + a.per);
@@ -137,6 +190,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_partial_kernel(const AttnArgs
     }
     fence_mbar_init();
   }
+  if (tid < HD) sm.zero[tid] = 0;
   __syncthreads();
 
   if (warp == N_CONSUMER) {
@@ -149,62 +203,99 @@ __global__ void __launch_bounds__(THREADS, 1) attn_partial_kernel(const AttnArgs
       if (i >= STAGES && !mbar_wait(&sm.empty[s], ((i / STAGES) - 1) & 1, a.err)) return;
       const TileInfo t = tile_info(a, c);
       if (t.page_id < 0) record_error(a.err, QC_ERR_BOUNDS);
-      const uint32_t bytes = (t.page_id >= 0) ? uint32_t(t.rows_cached) * HD * 2 : 0u;
-      mbar_arrive_expect_tx(&sm.full[s], 2 * bytes);
-      if (bytes) {
-        const int64_t off = ((int64_t)t.page_id * 4 + c.kvh) * PAGE * HD;
-        bulk_g2s(sm.k[s], a.k_pool + off, bytes, &sm.full[s]);
-        bulk_g2s(sm.v[s], a.v_pool + off, bytes, &sm.full[s]);
-      }
+      const int nbox = (t.page_id >= 0) ? (t.rows_cached + BOX_ROWS - 1) / BOX_ROWS : 0;
+      mbar_arrive_expect_tx(&sm.full[s], uint32_t(nbox * 4 * BOX_BYTES * 2));
+      const int row0 = (t.page_id * 4 + c.kvh) * PAGE;
+      for (int rb = 0; rb < nbox; ++rb)
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb) {
+          const int off = (cb * PAGE * 128 + rb * BOX_BYTES) / 2;
+          tma_load_2d(&sm.k[s][off], &tmk, cb * 64, row0 + rb * BOX_ROWS, &sm.full[s]);
+          tma_load_2d(&sm.v[s][off], &tmv, cb * 64, row0 + rb * BOX_ROWS, &sm.full[s]);
+        }
     }
     return;
   }
 
   // -------------------------------------------------------------- consumers
+  const int g = lane >> 2, t4 = lane & 3;
   Cursor c;
   c.seek(a, u_begin);
   bool aborted = false;
-  float q[4][8];
-  float o[4][8];
-  float m_run[4], l_run[4];
+  uint32_t qb[16][2];     // B fragments of Qx^T per 16-dim step
+  float oacc[16][4];      // O^T accumulators, m-tile mt = dims 16mt..16mt+15
+  float m_run[2], l_run[2];
   int cur_b = -1, cur_kvh = -1;
 
+  auto reset_state = [&]() {
+#pragma unroll
+    for (int mt = 0; mt < 16; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) oacc[mt][e] = 0.0f;
+    m_run[0] = m_run[1] = -INFINITY;
+    l_run[0] = l_run[1] = 0.0f;
+  };
+
   auto flush = [&]() {
-    if (lane == 0) {
+    // fold the lo columns into the hi columns: lanes t4 < 2 keep heads
+    // 2*t4, 2*t4 + 1
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        sm.red_ml[warp][h] = m_run[h];
-        sm.red_ml[warp][4 + h] = l_run[h];
-      }
-    }
+    for (int mt = 0; mt < 16; ++mt)
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      float4* dst = reinterpret_cast<float4*>(&sm.red_o[warp][h][lane * 8]);
-      dst[0] = make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
-      dst[1] = make_float4(o[h][4], o[h][5], o[h][6], o[h][7]);
+      for (int e = 0; e < 4; ++e) oacc[mt][e] += __shfl_xor_sync(FULL_MASK, oacc[mt][e], 2);
+    if (lane < 2) {
+      sm.red_ml[warp][2 * lane] = m_run[0];
+      sm.red_ml[warp][2 * lane + 1] = m_run[1];
+      sm.red_ml[warp][4 + 2 * lane] = l_run[0];
+      sm.red_ml[warp][4 + 2 * lane + 1] = l_run[1];
     }
     consumer_sync();
-    const int slot = cur_b * 4 + cur_kvh + blockIdx.x;
+    float M[4], L[4], acc[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-      float M = -INFINITY;
+      M[h] = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < N_CONSUMER; ++w) M = fmaxf(M, sm.red_ml[w][h]);
-      float O = 0.0f, L = 0.0f;
+      for (int w = 0; w < N_CONSUMER; ++w) M[h] = fmaxf(M[h], sm.red_ml[w][h]);
+      L[h] = 0.0f;
 #pragma unroll
       for (int w = 0; w < N_CONSUMER; ++w) {
         const float mw = sm.red_ml[w][h];
-        const float f = (mw == -INFINITY) ? 0.0f : exp2f(mw - M);
-        O = fmaf(f, sm.red_o[w][h][tid], O);
-        L = fmaf(f, sm.red_ml[w][4 + h], L);
+        if (mw != -INFINITY) L[h] = fmaf(exp2f(mw - M[h]), sm.red_ml[w][4 + h], L[h]);
       }
-      a.part_o[((int64_t)slot * 4 + h) * HD + tid] = O;
-      if (tid == 0) {
-        a.part_m[slot * 4 + h] = M;
-        a.part_l[slot * 4 + h] = L;
-      }
+      acc[h] = 0.0f;
     }
-    consumer_sync();
+    const int hA = 2 * (t4 & 1);
+    const float MA = (t4 & 1) ? M[2] : M[0], MB = (t4 & 1) ? M[3] : M[1];
+    const float fA = (m_run[0] == -INFINITY) ? 0.0f : exp2f(m_run[0] - MA);
+    const float fB = (m_run[1] == -INFINITY) ? 0.0f : exp2f(m_run[1] - MB);
+#pragma unroll
+    for (int grp = 0; grp < 2; ++grp) {
+      if ((warp >> 2) == grp && t4 < 2) {
+        float* roA = sm.red_o[warp & 3][hA];
+        float* roB = sm.red_o[warp & 3][hA + 1];
+#pragma unroll
+        for (int mt = 0; mt < 16; ++mt) {
+          const int d = 16 * mt + g;
+          roA[d] = oacc[mt][0] * fA;
+          roB[d] = oacc[mt][1] * fB;
+          roA[d + 8] = oacc[mt][2] * fA;
+          roB[d + 8] = oacc[mt][3] * fB;
+        }
+      }
+      consumer_sync();
+#pragma unroll
+      for (int w = 0; w < 4; ++w)
+#pragma unroll
+        for (int h = 0; h < 4; ++h) acc[h] += sm.red_o[w][h][tid];
+      consumer_sync();
+    }
+    const int slot = cur_b * 4 + cur_kvh + blockIdx.x;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) a.part_o[((int64_t)slot * 4 + h) * HD + tid] = acc[h];
+    if (tid < 4) {
+      a.part_m[slot * 4 + tid] = M[tid];
+      a.part_l[slot * 4 + tid] = L[tid];
+    }
   };
 
   for (int i = 0, u = u_begin; u < u_end; ++i, ++u, c.next(a)) {
@@ -243,10 +334,10 @@ __global__ void __launch_bounds__(THREADS, 1) attn_partial_kernel(const AttnArgs
           unpack8(*reinterpret_cast<const uint4*>(prow + 8192 + c.kvh * HD + lane * 8), x);
           norm_rope_lane(x, a.k_norm, cs, sn, lane);
           uint4 w;
-          w.x = uint32_t(f2bf(x[0])) | (uint32_t(f2bf(x[1])) << 16);
-          w.y = uint32_t(f2bf(x[2])) | (uint32_t(f2bf(x[3])) << 16);
-          w.z = uint32_t(f2bf(x[4])) | (uint32_t(f2bf(x[5])) << 16);
-          w.w = uint32_t(f2bf(x[6])) | (uint32_t(f2bf(x[7])) << 16);
+          w.x = pack_bf16(x[0], x[1]);
+          w.y = pack_bf16(x[2], x[3]);
+          w.z = pack_bf16(x[4], x[5]);
+          w.w = pack_bf16(x[6], x[7]);
           *reinterpret_cast<uint4*>(&sm.knew[lane * 8]) = w;
           if (in_bounds) *reinterpret_cast<uint4*>(a.k_pool + row_off) = w;
         } else {
@@ -257,17 +348,24 @@ __global__ void __launch_bounds__(THREADS, 1) attn_partial_kernel(const AttnArgs
         if (!in_bounds && lane == 0) record_error(a.err, QC_ERR_BOUNDS);
       }
       consumer_sync();
+      // B fragments of Qx^T: column g holds head g & 3, hi part for g < 4 and
+      // lo part for g >= 4; k-step j covers dims 16j..16j+15
+      {
+        const int hq = g & 3;
+        const bool lo_part = g >= 4;
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const float4 q0 = *reinterpret_cast<const float4*>(&sm.q[h][lane * 8]);
-        const float4 q1 = *reinterpret_cast<const float4*>(&sm.q[h][lane * 8 + 4]);
-        q[h][0] = q0.x; q[h][1] = q0.y; q[h][2] = q0.z; q[h][3] = q0.w;
-        q[h][4] = q1.x; q[h][5] = q1.y; q[h][6] = q1.z; q[h][7] = q1.w;
-        m_run[h] = -INFINITY;
-        l_run[h] = 0.0f;
+        for (int j = 0; j < 16; ++j)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[h][e] = 0.0f;
+          for (int e = 0; e < 2; ++e) {
+            const int d = 16 * j + 8 * e + 2 * t4;
+            uint16_t h0, l0, h1, l1;
+            split_bf16(sm.q[hq][d], h0, l0);
+            split_bf16(sm.q[hq][d + 1], h1, l1);
+            qb[j][e] = lo_part ? (uint32_t(l0) | (uint32_t(l1) << 16))
+                               : (uint32_t(h0) | (uint32_t(h1) << 16));
+          }
       }
+      reset_state();
     }
 
     if (!aborted && !mbar_wait(&sm.full[s], (i / STAGES) & 1, a.err)) aborted = true;
@@ -275,75 +373,79 @@ __global__ void __launch_bounds__(THREADS, 1) attn_partial_kernel(const AttnArgs
 
     const int r0 = warp * 8;
     if (r0 < t.tile_len) {
-      const uint16_t* kbase = sm.k[s];
-      const uint16_t* vbase = sm.v[s];
+      // this lane's ldmatrix row: position r0 + (lane & 7), 8-dim chunk lane >> 3
+      const int row = r0 + (lane & 7);
+      const int mi = lane >> 3;
       const int new_row = t.append_here ? t.rows_cached : -1;
-      float acc[32];
+      const bool plain = (row == new_row) || (row >= t.tile_len);
+      const uint32_t kb = (row == new_row) ? smem_u32(sm.knew)
+                          : (row >= t.tile_len) ? smem_u32(sm.zero) : smem_u32(sm.k[s]);
+      const uint32_t vb = (row == new_row) ? smem_u32(sm.vnew)
+                          : (row >= t.tile_len) ? smem_u32(sm.zero) : smem_u32(sm.v[s]);
+      // ---- S^T = K . Qx^T  (two accumulator chains)
+      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int row = r0 + j;
-        uint4 kw = make_uint4(0, 0, 0, 0);
-        if (row < t.tile_len) {
-          const uint16_t* kr = (row == new_row) ? sm.knew : kbase + row * HD;
-          kw = *reinterpret_cast<const uint4*>(kr + lane * 8);
-        }
-        float kf[8];
-        unpack8(kw, kf);
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          float d = q[h][0] * kf[0];
-#pragma unroll
-          for (int e = 1; e < 8; ++e) d = fmaf(q[h][e], kf[e], d);
-          acc[j * 4 + h] = d;
-        }
+      for (int jj = 0; jj < 8; ++jj) {
+        const int d = 32 * jj + 8 * mi;
+        const uint32_t addr = kb + (plain ? uint32_t(d * 2) : swz(row, d));
+        uint32_t m0, m1, m2, m3;
+        ldsm_x4(addr, m0, m1, m2, m3);
+        mma_k16(sa, m0, m1, qb[2 * jj][0], qb[2 * jj][1]);
+        mma_k16(sb, m2, m3, qb[2 * jj + 1][0], qb[2 * jj + 1][1]);
       }
-      const float dot = transpose_reduce32(acc, lane);
-      const int my_row = r0 + (lane >> 2);
-      const float sc = (my_row < t.tile_len) ? dot * SCALE_LOG2 : -INFINITY;
-      float mx = sc;
-      mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 4));
-      mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 8));
-      mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, 16));
-      float m_new[4], corr[4];
+      // lane (g, t4): position r0 + g, columns 2t4, 2t4 + 1 -> heads hA, hA + 1
+      float s0 = sa[0] + sb[0], s1 = sa[1] + sb[1];
+      s0 += __shfl_xor_sync(FULL_MASK, s0, 2);  // hi + lo columns
+      s1 += __shfl_xor_sync(FULL_MASK, s1, 2);
+      const bool valid = (r0 + g) < t.tile_len;
+      const float sc0 = valid ? s0 * SCALE_LOG2 : -INFINITY;
+      const float sc1 = valid ? s1 * SCALE_LOG2 : -INFINITY;
+      float mx0 = sc0, mx1 = sc1;
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        m_new[h] = fmaxf(m_run[h], __shfl_sync(FULL_MASK, mx, h));
-        corr[h] = (m_new[h] == -INFINITY) ? 1.0f : exp2f(m_run[h] - m_new[h]);
+      for (int m = 4; m <= 16; m <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(FULL_MASK, mx0, m));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(FULL_MASK, mx1, m));
       }
-      const int hl = lane & 3;
-      const float my_m = hl == 0 ? m_new[0] : hl == 1 ? m_new[1] : hl == 2 ? m_new[2] : m_new[3];
-      const float p = (sc == -INFINITY) ? 0.0f : exp2f(sc - my_m);
-      float ps = p;
-      ps += __shfl_xor_sync(FULL_MASK, ps, 4);
-      ps += __shfl_xor_sync(FULL_MASK, ps, 8);
-      ps += __shfl_xor_sync(FULL_MASK, ps, 16);
+      const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
+      const float c0 = (mn0 == -INFINITY) ? 1.0f : exp2f(m_run[0] - mn0);
+      const float c1 = (mn1 == -INFINITY) ? 1.0f : exp2f(m_run[1] - mn1);
+      const float p0 = (sc0 == -INFINITY) ? 0.0f : exp2f(sc0 - mn0);
+      const float p1 = (sc1 == -INFINITY) ? 0.0f : exp2f(sc1 - mn1);
+      float ps0 = p0, ps1 = p1;
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        l_run[h] = fmaf(l_run[h], corr[h], __shfl_sync(FULL_MASK, ps, h));
-        m_run[h] = m_new[h];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[h][e] *= corr[h];
+      for (int m = 4; m <= 16; m <<= 1) {
+        ps0 += __shfl_xor_sync(FULL_MASK, ps0, m);
+        ps1 += __shfl_xor_sync(FULL_MASK, ps1, m);
       }
-      sm.p[warp][lane] = p;
-      __syncwarp();
+      l_run[0] = fmaf(l_run[0], c0, ps0);
+      l_run[1] = fmaf(l_run[1], c1, ps1);
+      m_run[0] = mn0;
+      m_run[1] = mn1;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int row = r0 + j;
-        if (row < t.tile_len) {
-          const uint16_t* vr = (row == new_row) ? sm.vnew : vbase + row * HD;
-          float vf[8];
-          unpack8(*reinterpret_cast<const uint4*>(vr + lane * 8), vf);
-          const float4 pj = *reinterpret_cast<const float4*>(&sm.p[warp][j * 4]);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            o[0][e] = fmaf(pj.x, vf[e], o[0][e]);
-            o[1][e] = fmaf(pj.y, vf[e], o[1][e]);
-            o[2][e] = fmaf(pj.z, vf[e], o[2][e]);
-            o[3][e] = fmaf(pj.w, vf[e], o[3][e]);
-          }
-        }
+      for (int mt = 0; mt < 16; ++mt) {
+        oacc[mt][0] *= c0;
+        oacc[mt][1] *= c1;
+        oacc[mt][2] *= c0;
+        oacc[mt][3] *= c1;
       }
-      __syncwarp();
+      // ---- Px^T B fragment: matrix [pos g][col], col 2t4, 2t4+1 = hi (t4 < 2)
+      // or lo (t4 >= 2) parts of p for heads hA, hA + 1; transpose with movmatrix
+      uint16_t h0, l0, h1, l1;
+      split_bf16(p0, h0, l0);
+      split_bf16(p1, h1, l1);
+      const uint32_t pm = (t4 < 2) ? (uint32_t(h0) | (uint32_t(h1) << 16))
+                                   : (uint32_t(l0) | (uint32_t(l1) << 16));
+      const uint32_t pb = movmatrix_t(pm);
+      // ---- O^T += V^T . Px^T
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const int d = 32 * jj + 8 * mi;
+        const uint32_t addr = vb + (plain ? uint32_t(d * 2) : swz(row, d));
+        uint32_t v0, v1, v2, v3;
+        ldsm_x4_t(addr, v0, v1, v2, v3);
+        mma_k8(oacc[2 * jj], v0, v1, pb);
+        mma_k8(oacc[2 * jj + 1], v2, v3, pb);
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[s]);
@@ -378,19 +480,22 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const CombineArgs c) 
 
 }  // namespace
 
-int attn_smem_bytes() { return static_cast<int>(sizeof(Smem)); }
+int attn_smem_bytes() { return static_cast<int>(sizeof(Smem)) + 1024; }
 
-cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, cudaStream_t s) {
+cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CUtensorMap& tmk,
+                               const CUtensorMap& tmv, cudaStream_t s) {
   if (a.n <= 0 || a.total <= 0) return cudaSuccess;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
     cudaError_t e = cudaFuncSetAttribute(attn_partial_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          attn_smem_bytes());
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    configured_device = dev;
   }
-  attn_partial_kernel<<<a.grid, THREADS, attn_smem_bytes(), s>>>(a);
+  attn_partial_kernel<<<a.grid, THREADS, attn_smem_bytes(), s>>>(a, tmk, tmv);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   attn_combine_kernel<<<c.n * 4, 256, 0, s>>>(c);

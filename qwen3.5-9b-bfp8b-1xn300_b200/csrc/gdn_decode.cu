@@ -17,7 +17,7 @@
 //      with 128-bit stores;
 //   5. gated RMSNorm over the head's 128 outputs (for R > 1 the CTAs of the
 //      cluster exchange their partial sums of squares through distributed
-//      shared memory, plain stores, no multicast), then bf16 outputs.
+//      shared memory with plain stores), then bf16 outputs.
 // HBM traffic per (sequence, layer): state 2 MiB read + 2 MiB written, conv
 // ring 3 x 16 KiB read + 16 KiB written, projection row 24.7 KB, output 8 KB.
 //

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace qc {
@@ -64,7 +65,10 @@ struct CombineArgs {
   int32_t n;
   int32_t per;
 };
-cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, cudaStream_t s);
+// tmk / tmv: 2D tensor maps over this layer's K / V pool viewed as
+// [max_pages * 4 * 64 rows][256 bf16], box 16 rows x 64 columns, 128 B swizzle.
+cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CUtensorMap& tmk,
+                               const CUtensorMap& tmv, cudaStream_t s);
 int attn_smem_bytes();
 
 // Copies (kv_copy.cu).

@@ -19,6 +19,8 @@
 #include <unordered_map>
 #include <vector>
 
+#include <cudaTypedefs.h>
+
 #include "../../include/qcache.h"
 #include "kernels.h"
 
@@ -86,6 +88,7 @@ struct qc_ctx {
   int64_t* chunk_start = nullptr;
   int32_t job_cap = 0;
   int* dev_err = nullptr;
+  std::vector<CUtensorMap> tm_k, tm_v;  // per attention layer, for the TMA tile loads
 
   // pinned staging ring for host -> device uploads
   char* stage[STAGING_SLOTS] = {};
@@ -369,6 +372,30 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
     if ((e = cudaMemcpy(c->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice)) ||
         (e = cudaMemcpy(c->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice)))
       return cuda_fail(e, "rope upload");
+  }
+  // TMA tensor maps over each layer's K and V pool: [rows][256] bf16 with
+  // rows = max_pages * 4 kv-heads * 64 positions, 16 x 64 boxes, 128 B swizzle
+  {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", (void**)&encode, cudaEnableDefault, &qres);
+    if (e != cudaSuccess || !encode || qres != cudaDriverEntryPointSuccess)
+      return cuda_fail(e != cudaSuccess ? e : cudaErrorNotSupported, "cuTensorMapEncodeTiled");
+    c->tm_k.resize(na);
+    c->tm_v.resize(na);
+    const cuuint64_t dims[2] = {(cuuint64_t)HD, (cuuint64_t)cfg->max_pages * QC_N_HEAD_KV * PAGE};
+    const cuuint64_t strides[1] = {(cuuint64_t)HD * 2};
+    const cuuint32_t box[2] = {64, 16};
+    const cuuint32_t estr[2] = {1, 1};
+    for (int l = 0; l < na; ++l)
+      for (int kv = 0; kv < 2; ++kv) {
+        uint16_t* base = (kv ? c->v_pool : c->k_pool) + (int64_t)l * cfg->max_pages * PAGE_ELEMS;
+        CUresult r = encode(kv ? &c->tm_v[l] : &c->tm_k[l], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                            base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return cuda_fail(cudaErrorInvalidValue, "tensor map encode");
+      }
   }
   c->stage_cap = std::max<size_t>((size_t)(5 * cfg->max_batch + 8) * 4 +
                                       (size_t)c->pt_stride * 4,
@@ -702,7 +729,7 @@ int qc_attn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc
   cb.part_o = c->part_o;
   cb.n = n;
   cb.per = c->b_per;
-  QC_CUDA(c, qc::launch_attn_decode(a, cb, (cudaStream_t)stream));
+  QC_CUDA(c, qc::launch_attn_decode(a, cb, c->tm_k[layer], c->tm_v[layer], (cudaStream_t)stream));
   return QC_OK;
 }
 
