@@ -134,22 +134,24 @@ class ClockSampler:
 
 
 class Stack:
-    """The 32-layer cache stack for this rank's n sequences on one GPU."""
+    """A cache stack for this rank's n sequences on one GPU: `kinds` lists the
+    layers in order ("a" attention, "g" DeltaNet)."""
 
-    def __init__(self, qc, synth, torch, n, ctx, extra_tokens, seed, stream):
-        self.torch, self.n, self.ctx = torch, n, ctx
+    def __init__(self, qc, synth, torch, kinds, n, ctx, extra_tokens, seed, stream):
+        self.torch, self.n, self.ctx, self.kinds = torch, n, ctx, kinds
         self.stream = stream
+        n_attn, n_gdn = kinds.count("a"), kinds.count("g")
         pages_per_seq = (ctx + extra_tokens) // 64 + 1
-        self.q = qc.QCache(n_attn_layers=N_ATTN, n_gdn_layers=N_GDN, max_seqs=n,
+        self.q = qc.QCache(n_attn_layers=n_attn, n_gdn_layers=n_gdn, max_seqs=n,
                            max_pages=n * pages_per_seq, max_ctx=ctx + extra_tokens + 64,
                            max_batch=n, max_snapshots=1, device=torch.cuda.current_device())
         q = self.q
         g = torch.Generator(device="cuda")
         g.manual_seed(seed)
-        for l in range(N_ATTN):
+        for l in range(n_attn):
             a = synth.attn_inputs(seed + l, 1, 0)
             q.set_attn_params(l, a["q_norm"], a["k_norm"])
-        for l in range(N_GDN):
+        for l in range(n_gdn):
             p = synth.gdn_params(seed + 100 + l)
             q.set_gdn_params(l, p["ssm_a"], p["dt_bias"], p["ssm_norm"], p["conv_w"])
         self.seqs = [q.seq_alloc() for _ in range(n)]
@@ -163,33 +165,37 @@ class Stack:
             q.seq_reserve(s, min(ctx, have[s] * 64))
         bf16 = torch.bfloat16
         for s in self.seqs:
-            for l in range(N_ATTN):
+            for l in range(n_attn):
                 k = torch.randn(ctx, 4, 256, generator=g, device="cuda").to(bf16)
                 v = torch.randn(ctx, 4, 256, generator=g, device="cuda").to(bf16)
                 q.kv_write(s, l, 0, ctx, k.data_ptr(), v.data_ptr(), stream)
                 torch.cuda.synchronize()
-            for l in range(N_GDN):
+            for l in range(n_gdn):
                 st = torch.randn(32, 128, 128, generator=g, device="cuda") * 0.02
                 hi = torch.randn(3, 8192, generator=g, device="cuda").to(bf16)
                 q.gdn_state_write(s, l, st.data_ptr(), hi.data_ptr(), stream)
                 torch.cuda.synchronize()
         # per-layer projection inputs and outputs
         self.proj = []
-        for layer in range(N_LAYERS):
-            w = 10240 if is_attn(layer) else 12352
+        for kind in kinds:
+            w = 10240 if kind == "a" else 12352
             self.proj.append(torch.randn(n, w, generator=g, device="cuda").to(bf16))
-        self.out = [torch.empty(n, 4096, device="cuda", dtype=bf16) for _ in range(N_LAYERS)]
+        self.out = [torch.empty(n, 4096, device="cuda", dtype=bf16) for _ in kinds]
         torch.cuda.synchronize()
         q.check_device()
 
     def step(self, events=None):
-        q, st = self.q, self.stream
-        q.decode_begin(self.seqs, stream=st)
+        self.q.decode_begin(self.seqs, stream=self.stream)
+        self.layers(self.stream, events)
+        self.q.decode_end()
+
+    def layers(self, st, events=None):
+        q = self.q
         ai = gi = 0
-        for layer in range(N_LAYERS):
+        for layer, kind in enumerate(self.kinds):
             if events is not None:
                 events[layer][0].record()
-            if is_attn(layer):
+            if kind == "a":
                 q.attn_decode(ai, self.proj[layer].data_ptr(), self.out[layer].data_ptr(), st)
                 ai += 1
             else:
@@ -197,7 +203,6 @@ class Stack:
                 gi += 1
             if events is not None:
                 events[layer][1].record()
-        q.decode_end()
 
     def step_bytes(self):
         """Algorithmic HBM bytes of ONE layer launch of each type in the next
@@ -208,16 +213,38 @@ class Stack:
         return attn, gdn
 
 
-def run_ours(args, rank, world, dist):
+WORKLOADS = {
+    # name: (layer kinds, total sequences, context, description)
+    "stack": ([("a" if is_attn(l) else "g") for l in range(N_LAYERS)], N_SEQ, CTX,
+              "full cache stack: 24 DeltaNet + 8 attention layers (attention every 4th), "
+              "{n} sequences at context {ctx}, 64-token bf16 pages (permuted), one decode "
+              "token per sequence"),
+    "gdn": (["g"] * N_GDN, 64, 0,
+            "Gated DeltaNet decode step, 24 layers, batch {n}: fp32 state [32,128,128], "
+            "conv ring, gated RMSNorm"),
+    "attn": (["a"], 1, 1024,
+             "single full-attention layer decode, batch {n}, {ctx} cached positions, fused "
+             "Q/K norm + RoPE + append, L2 flushed between steps"),
+    "long": (["a"] * N_ATTN, 1, 131072,
+             "long-context single sequence: 8 attention layers at context {ctx}, split-K "
+             "over KV pages"),
+}
+
+
+def run_ours(args, rank, world, dist, kinds, n_total, ctx):
     import torch
     qc = load_pkg("qcache")
     synth = load_pkg("synth")
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    n = args.seqs // world
+    n = n_total // world
     stream = torch.cuda.current_stream().cuda_stream
-    stack = Stack(qc, synth, torch, n, CTX, args.warmup + args.steps + 8, seed=1000 + rank,
-                  stream=stream)
+    stack = Stack(qc, synth, torch, kinds, n, ctx, args.warmup + args.steps + 8,
+                  seed=1000 + rank, stream=stream)
+    nl = len(kinds)
+    # inputs smaller than L2 (126 MB): flush it between steps, outside the events
+    small = ctx * 4096 * kinds.count("a") * n + n * 2 ** 21 * 2 * kinds.count("g") < 512 * 2 ** 20
+    flush_buf = torch.empty(512 * 2 ** 20, dtype=torch.uint8, device="cuda") if small else None
 
     def barrier():
         if dist is not None:
@@ -228,10 +255,26 @@ def run_ours(args, rank, world, dist):
         stack.step()
     barrier()
 
-    # ---- device-timed region: K steps, per-layer events for the roofline
+    # ---- capture the layer calls of one step into a CUDA graph (the
+    # per-step inputs -- positions, split sizes -- are read from the device
+    # descriptor that qc_decode_begin uploads, so the graph replays every step)
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    stack.q.decode_begin(stack.seqs, stream=stream)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph, stream=cap):
+        stack.layers(torch.cuda.current_stream().cuda_stream)
+    stack.q.decode_abort()
+    torch.cuda.synchronize()
+
+    def graph_step():
+        stack.q.decode_begin(stack.seqs, stream=stream)
+        graph.replay()
+        stack.q.decode_end()
+
+    # ---- device-timed region: K graph steps
     attn_b = gdn_b = 0
-    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(N_LAYERS)]
-          for _ in range(args.steps)]
+    sev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.5)   # let the sampler come up before the timed region
@@ -243,15 +286,35 @@ def run_ours(args, rank, world, dist):
         a, g_ = stack.step_bytes()
         attn_b += a
         gdn_b += g_
-        stack.step(ev[k])
+        if flush_buf is not None:
+            flush_buf.zero_()
+        sev[k][0].record()
+        graph_step()
+        sev[k][1].record()
     t1.record()
     barrier()
     clk = clocks.stop()
-    ms = t0.elapsed_time(t1) / args.steps
-    attn_ms = sum(ev[k][l][0].elapsed_time(ev[k][l][1]) for k in range(args.steps)
-                  for l in range(N_LAYERS) if is_attn(l)) / args.steps
-    gdn_ms = sum(ev[k][l][0].elapsed_time(ev[k][l][1]) for k in range(args.steps)
-                 for l in range(N_LAYERS) if not is_attn(l)) / args.steps
+    # with L2 flushes inside the region, the step time is the sum of the steps
+    ms = (sum(e0.elapsed_time(e1) for e0, e1 in sev) / args.steps if small
+          else t0.elapsed_time(t1) / args.steps)
+    # per-layer-type split: with one layer type it is the step; otherwise a few
+    # extra non-graph steps with an event pair around every layer call (the
+    # GPU stays saturated in these workloads, so the split is device time)
+    if kinds.count("a") == 0 or kinds.count("g") == 0:
+        attn_ms = ms if kinds.count("a") else 0.0
+        gdn_ms = ms if kinds.count("g") else 0.0
+    else:
+        ks = min(args.steps, 10)
+        ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(nl)]
+              for _ in range(ks)]
+        for k in range(ks):
+            stack.step(ev[k])
+        torch.cuda.synchronize()
+        lt = [sum(ev[k][l][0].elapsed_time(ev[k][l][1]) for k in range(ks)) / ks
+              for l in range(nl)]
+        tot = sum(lt)
+        attn_ms = ms * sum(t for t, kd in zip(lt, kinds) if kd == "a") / tot
+        gdn_ms = ms * sum(t for t, kd in zip(lt, kinds) if kd == "g") / tot
     stack.q.check_device()
 
     # ---- end-to-end through the C ABI with host buffers
@@ -268,7 +331,7 @@ def run_ours(args, rank, world, dist):
     for _ in range(e2e_steps):
         for p, h in zip(stack.proj, h_in):
             p.copy_(h, non_blocking=True)
-        stack.step()
+        graph_step()
         for o, h in zip(stack.out, h_out):
             h.copy_(o, non_blocking=True)
     e1.record()
@@ -281,8 +344,9 @@ def run_ours(args, rank, world, dist):
     ms, e2e_ms, attn_ms, gdn_ms = vals.tolist()
     return dict(ms=ms, e2e_ms=e2e_ms, attn_ms=attn_ms, gdn_ms=gdn_ms,
                 attn_layer_bytes=attn_b / args.steps, gdn_layer_bytes=gdn_b / args.steps,
-                n_local=n,
-                h2d=h2d, d2h=d2h, clocks=clk)
+                n_local=n, h2d=h2d, d2h=d2h, clocks=clk,
+                l2="L2 flushed (512 MB write) between steps" if small
+                else "inputs larger than L2 (126 MB) on every step")
 
 
 # ------------------------------------------------------------ CPU baseline
@@ -357,20 +421,27 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
-    ap.add_argument("--seqs", type=int, default=N_SEQ,
-                    help="total sequences (smaller values only for profiling captures)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(WORKLOADS), default="stack",
+                    help="stack = the headline workload; the others are the baseline's "
+                         "per-component configurations")
+    ap.add_argument("--seqs", type=int, default=None,
+                    help="total sequences (default: the configuration's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    workload = (f"full cache stack: 24 DeltaNet + 8 attention layers, {args.seqs} sequences at "
-                f"context {CTX}, 64-token bf16 pages (permuted), 1 decode token per sequence")
-    config = {"workload": workload, "sequences": args.seqs, "context": CTX, "layers": N_LAYERS,
-              "page_tokens": 64, "timing": "CUDA events on the launching stream, max over ranks",
-              "sharding": f"sequences over {world} GPU(s), no collective",
-              "l2": "inputs larger than L2 (~15 GB of KV/state per step)"}
+    kinds, n_total, ctx, desc = WORKLOADS[args.config]
+    if args.seqs:
+        n_total = args.seqs
+    n_attn, n_gdn = kinds.count("a"), kinds.count("g")
+    config = {"workload": desc.format(n=n_total, ctx=ctx), "name": args.config,
+              "sequences": n_total, "context": ctx, "layers": len(kinds),
+              "attention_layers": n_attn, "deltanet_layers": n_gdn, "page_tokens": 64,
+              "timing": "CUDA events on the launching stream, max over ranks; each step = "
+                        "qc_decode_begin + CUDA-graph replay of the layer calls + qc_decode_end",
+              "sharding": f"sequences over {world} GPU(s), no collective"}
     metric = "decode cache-path us/token/layer"
 
     if args.impl == "reference":
@@ -393,7 +464,7 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         dist_mod.init_process_group("nccl")
         dist = dist_mod
-    r = run_ours(args, rank, world, dist)
+    r = run_ours(args, rank, world, dist, kinds, n_total, ctx)
     if dist is not None:
         dist.barrier()
     if rank != 0:
@@ -401,19 +472,20 @@ def main():
             dist.destroy_process_group()
         return
     peak, peak_kind = measured_peaks()
-    units = args.seqs * N_LAYERS
+    units = n_total * len(kinds)
     us = r["ms"] * 1e3 / units
     # every rank holds the same number of sequences at the same context
-    step_bytes = (N_ATTN * r["attn_layer_bytes"] + N_GDN * r["gdn_layer_bytes"]) * world
+    step_bytes = (n_attn * r["attn_layer_bytes"] + n_gdn * r["gdn_layer_bytes"]) * world
     gbs = step_bytes / (r["ms"] * 1e-3) / 1e9
+    config["l2"] = r["l2"]
     # dominant kernel: the layer type with the larger device time per step;
     # achieved = its algorithmic bytes per launch / its average launch time
     if r["attn_ms"] >= r["gdn_ms"]:
         kname, kbytes, kms = ("attn_partial_kernel + attn_combine_kernel (one attention layer)",
-                              r["attn_layer_bytes"], r["attn_ms"] / N_ATTN)
+                              r["attn_layer_bytes"], r["attn_ms"] / n_attn)
     else:
-        kname, kbytes, kms = ("gdn_decode_kernel (one DeltaNet layer)", r["gdn_layer_bytes"],
-                              r["gdn_ms"] / N_GDN)
+        kname, kbytes, kms = ("gdn_decode (one DeltaNet layer)", r["gdn_layer_bytes"],
+                              r["gdn_ms"] / n_gdn)
     k_gbs = kbytes / (kms * 1e-3) / 1e9
     line = {
         "metric": metric, "value": round(us, 4), "unit": "us", "n_gpus": world,
@@ -423,14 +495,14 @@ def main():
         "hbm": {"algorithmic_bytes_per_step": int(step_bytes), "achieved_gbs": round(gbs, 1),
                 "frac_of_8tbs": round(gbs / world / HBM_NOMINAL_GBS, 4),
                 "frac_of_measured": round(gbs / world / peak, 4)},
-        "layer_time_ms": {"attention_8_layers": round(r["attn_ms"], 4),
-                          "deltanet_24_layers": round(r["gdn_ms"], 4)},
+        "layer_time_ms": {"attention_total": round(r["attn_ms"], 4),
+                          "deltanet_total": round(r["gdn_ms"], 4)},
         "roofline": {"kernel": kname, "bound": "hbm", "achieved": round(k_gbs, 1),
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": round(k_gbs / peak, 4), "traffic": None},
         "e2e": {"value": round(r["e2e_ms"] * 1e3 / units, 4), "unit": "us",
                 "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
-        "gpu_launches": args.steps * (N_GDN + 2 * N_ATTN),
+        "gpu_launches": args.steps * (n_gdn + 2 * n_attn),
         "clocks": r["clocks"],
     }
     if not args.no_cpu_baseline and world == 1:

@@ -150,6 +150,14 @@ int qc_gdn_decode(qc_ctx* ctx, int gdn_layer, const uint16_t* proj_dev, uint16_t
 /* Commit the token: len(seq) += 1 for every sequence of the batch (g_pos++,
  * src/engine.cpp:4150). */
 int qc_decode_end(qc_ctx* ctx);
+/* Close the open step without committing the token (lengths and token
+ * histories unchanged; a page mapped for the position stays mapped).  Used
+ * after capturing the layer calls of a step into a CUDA graph, and to abandon
+ * a step after an error.  The layer calls read the step's positions and split
+ * sizes from device memory written by qc_decode_begin, so a captured graph of
+ * them replays correctly after every later qc_decode_begin for the same
+ * sequence list. */
+int qc_decode_abort(qc_ctx* ctx);
 
 /* ----------------------------------------------------------- prefix cache */
 

@@ -159,16 +159,22 @@ struct TileInfo {
   int tile_len;
 };
 
-__device__ __forceinline__ TileInfo tile_info(const AttnArgs& a, const Cursor& c) {
+// Rows of the tile; with_page also resolves the physical page through the
+// page table (the producer's job; consumers do not need it).
+__device__ __forceinline__ TileInfo tile_info(const AttnArgs& a, const Cursor& c,
+                                              bool with_page) {
   TileInfo t;
   const int page_abs = a.page0[c.b] + c.pg;
   const int pos = a.pos[c.b];
   const int start = page_abs * PAGE;
   t.rows_cached = min(max(pos - start, 0), PAGE);
   t.append_here = (a.append[c.b] && pos >= start && pos < start + PAGE) ? 1 : 0;
-  const int pid = a.page_table[(int64_t)a.slots[c.b] * a.pt_stride + page_abs];
-  t.page_id = (pid >= 0 && pid < a.max_pages) ? pid : -1;
-  t.tile_len = (t.page_id >= 0) ? t.rows_cached + t.append_here : 0;
+  t.page_id = 0;
+  if (with_page) {
+    const int pid = a.page_table[(int64_t)a.slots[c.b] * a.pt_stride + page_abs];
+    t.page_id = (pid >= 0 && pid < a.max_pages) ? pid : -1;
+  }
+  t.tile_len = t.rows_cached + t.append_here;
   return t;
 }
 
@@ -179,8 +185,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                       ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int u_begin = blockIdx.x * a.per;
-  const int u_end = min(a.total, u_begin + a.per);
+  const int total = a.split[0], per = a.split[1];
+  const int u_begin = blockIdx.x * per;
+  const int u_end = min(total, u_begin + per);
   if (u_begin >= u_end) return;
 
   if (tid == 0) {
@@ -195,24 +202,46 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == N_CONSUMER) {
     // ------------------------------------------------------------ producer
-    if (lane != 0) return;
-    Cursor c;
-    c.seek(a, u_begin);
-    for (int i = 0, u = u_begin; u < u_end; ++i, ++u, c.next(a)) {
-      const int s = i % STAGES;
-      if (i >= STAGES && !mbar_wait(&sm.empty[s], ((i / STAGES) - 1) & 1, a.err)) return;
-      const TileInfo t = tile_info(a, c);
-      if (t.page_id < 0) record_error(a.err, QC_ERR_BOUNDS);
-      const int nbox = (t.page_id >= 0) ? (t.rows_cached + BOX_ROWS - 1) / BOX_ROWS : 0;
-      mbar_arrive_expect_tx(&sm.full[s], uint32_t(nbox * 4 * BOX_BYTES * 2));
-      const int row0 = (t.page_id * 4 + c.kvh) * PAGE;
-      for (int rb = 0; rb < nbox; ++rb)
+    // Lane j resolves the page of tile base + j (page-table reads for 32 tiles
+    // in flight at once), lane 0 then waits for free stages and issues the
+    // TMA loads in order.
+    int i = 0;
+    for (int base = u_begin; base < u_end; base += 32) {
+      const int u = base + lane;
+      int pid = -1, rows = 0, kvh = 0;
+      if (u < u_end) {
+        Cursor c;
+        c.seek(a, u);
+        const TileInfo t = tile_info(a, c, true);
+        pid = t.page_id;
+        rows = t.rows_cached;
+        kvh = c.kvh;
+      }
+      const int cnt = min(32, u_end - base);
+      for (int j = 0; j < cnt; ++j, ++i) {
+        const int pj = __shfl_sync(FULL_MASK, pid, j);
+        const int rj = __shfl_sync(FULL_MASK, rows, j);
+        const int kj = __shfl_sync(FULL_MASK, kvh, j);
+        int ok = 1;
+        if (lane == 0) {
+          const int s = i % STAGES;
+          if (i >= STAGES && !mbar_wait(&sm.empty[s], ((i / STAGES) - 1) & 1, a.err)) ok = 0;
+          if (ok) {
+            if (pj < 0) record_error(a.err, QC_ERR_BOUNDS);
+            const int nbox = (pj >= 0) ? (rj + BOX_ROWS - 1) / BOX_ROWS : 0;
+            mbar_arrive_expect_tx(&sm.full[s], uint32_t(nbox * 4 * BOX_BYTES * 2));
+            const int row0 = (pj * 4 + kj) * PAGE;
+            for (int rb = 0; rb < nbox; ++rb)
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
-          const int off = (cb * PAGE * 128 + rb * BOX_BYTES) / 2;
-          tma_load_2d(&sm.k[s][off], &tmk, cb * 64, row0 + rb * BOX_ROWS, &sm.full[s]);
-          tma_load_2d(&sm.v[s][off], &tmv, cb * 64, row0 + rb * BOX_ROWS, &sm.full[s]);
+              for (int cb = 0; cb < 4; ++cb) {
+                const int off = (cb * PAGE * 128 + rb * BOX_BYTES) / 2;
+                tma_load_2d(&sm.k[s][off], &tmk, cb * 64, row0 + rb * BOX_ROWS, &sm.full[s]);
+                tma_load_2d(&sm.v[s][off], &tmv, cb * 64, row0 + rb * BOX_ROWS, &sm.full[s]);
+              }
+          }
         }
+        if (!__shfl_sync(FULL_MASK, ok, 0)) return;
+      }
     }
     return;
   }
@@ -300,7 +329,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   for (int i = 0, u = u_begin; u < u_end; ++i, ++u, c.next(a)) {
     const int s = i % STAGES;
-    const TileInfo t = tile_info(a, c);
+    const TileInfo t = tile_info(a, c, false);
     if (c.b != cur_b || c.kvh != cur_kvh) {
       if (cur_b >= 0) flush();
       cur_b = c.b;
@@ -458,7 +487,8 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const CombineArgs c) 
   const int b = pair >> 2, kvh = pair & 3, t = threadIdx.x;
   const int np = (c.seg[b + 1] - c.seg[b]) >> 2;
   const int u0 = c.seg[b] + kvh * np;
-  const int c0 = u0 / c.per, c1 = (u0 + np - 1) / c.per;
+  const int per = c.split[1];
+  const int c0 = u0 / per, c1 = (u0 + np - 1) / per;
   const uint16_t* prow = c.proj + (int64_t)b * 10240;
 #pragma unroll
   for (int hh = 0; hh < 4; ++hh) {
@@ -484,7 +514,7 @@ int attn_smem_bytes() { return static_cast<int>(sizeof(Smem)) + 1024; }
 
 cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CUtensorMap& tmk,
                                const CUtensorMap& tmv, cudaStream_t s) {
-  if (a.n <= 0 || a.total <= 0) return cudaSuccess;
+  if (a.n <= 0) return cudaSuccess;
   static int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);

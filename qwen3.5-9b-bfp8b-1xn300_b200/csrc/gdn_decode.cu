@@ -1,9 +1,9 @@
 // gdn_decode.cu — one Gated-DeltaNet decode step, fused in a single
 // memory-bound pass (src/engine.cpp:3204-3327).
 //
-// Work split: R CTAs per (sequence, v-head) — R = 1 (one 256-thread CTA per
-// head) for large batches, a cluster of R = 8 for batches of at most 8, which
-// would otherwise leave most of the 148 SMs idle.  CTA r owns state rows
+// Work split, small batches (at most 8 sequences): a cluster of R = 8 CTAs per
+// (sequence, v-head), which would otherwise leave most of the 148 SMs idle.
+// Large batches use the persistent producer/consumer kernel further down.  CTA r owns state rows
 // [r*128/R, (r+1)*128/R) of the head (rows are independent in the delta rule,
 // src/engine.cpp:3284-3305).  The CTA
 //   1. starts one bulk copy (TMA, cp.async.bulk) of its 128/R x 512 B state
@@ -223,6 +223,194 @@ __global__ void __launch_bounds__(T) gdn_decode_kernel(const GdnArgs a) {
   }
 }
 
+// Persistent variant for large batches: every CTA walks work items (one
+// (sequence, v-head) each) with stride gridDim.x.  Warp 8 streams the state of
+// its items in 32-row chunks (16 KiB bulk copies) through a PSTAGES-deep ring,
+// running ahead across item boundaries, so HBM stays busy while warps 0-7 run
+// the conv prologue, the delta rule and the gated RMSNorm of the current head.
+constexpr int PCHUNK = 32;                 // rows per chunk
+constexpr int PSTAGES = 6;
+constexpr int PCONSUMERS = 8;
+constexpr int PTHREADS = (PCONSUMERS + 1) * 32;
+
+struct PSmem {
+  float st[PSTAGES][PCHUNK * HK];
+  float q[HK];
+  float k[HK];
+  float v[HK];
+  float z[HK];
+  float o[HK];
+  float red[2 * PCONSUMERS];
+  uint64_t full[PSTAGES];
+  uint64_t empty[PSTAGES];
+};
+
+__device__ __forceinline__ void pconsumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(PCONSUMERS * 32) : "memory");
+}
+
+__global__ void __launch_bounds__(PTHREADS, 2) gdn_decode_persistent(const GdnArgs a) {
+  extern __shared__ __align__(128) unsigned char praw[];
+  PSmem& sm = *reinterpret_cast<PSmem*>(praw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_items = a.n * 32;
+  if (tid == 0) {
+    for (int s = 0; s < PSTAGES; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], PCONSUMERS);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == PCONSUMERS) {  // ------------------------------------ producer
+    if (lane != 0) return;
+    int i = 0;
+    for (int u = blockIdx.x; u < n_items; u += gridDim.x) {
+      const int b = u >> 5, vh = u & 31;
+      const float* src = a.state + a.slots[b] * a.state_stride + (int64_t)vh * HK * HK;
+      for (int j = 0; j < HK / PCHUNK; ++j, ++i) {
+        const int s = i % PSTAGES;
+        if (i >= PSTAGES && !mbar_wait(&sm.empty[s], ((i / PSTAGES) - 1) & 1, a.err)) return;
+        mbar_arrive_expect_tx(&sm.full[s], PCHUNK * HK * 4);
+        bulk_g2s(sm.st[s], src + j * PCHUNK * HK, PCHUNK * HK * 4, &sm.full[s]);
+      }
+    }
+    return;
+  }
+
+  // ----------------------------------------------------------------- consumers
+  bool aborted = false;
+  int i = 0;
+  const float* w = a.conv_w;
+  for (int u = blockIdx.x; u < n_items; u += gridDim.x) {
+    const int b = u >> 5, vh = u & 31, kh = vh & 15;
+    const int slot = a.slots[b], pos = a.pos[b];
+    uint16_t* ring = a.ring + slot * a.ring_stride;
+    const uint16_t* x = a.proj + (int64_t)b * 12352;
+    float* st = a.state + slot * a.state_stride + (int64_t)vh * HK * HK;
+    const int t0 = (pos - 3) & 3, t1 = (pos - 2) & 3, t2 = (pos - 1) & 3, tw = pos & 3;
+    auto conv1 = [&](int c) -> float {
+      float y = bf2f(ring[t0 * CONV + c]) * w[c];
+      y = fmaf(bf2f(ring[t1 * CONV + c]), w[CONV + c], y);
+      y = fmaf(bf2f(ring[t2 * CONV + c]), w[2 * CONV + c], y);
+      y = fmaf(bf2f(x[c]), w[3 * CONV + c], y);
+      return silu_exact(y);
+    };
+    // ---- prologue: conv + SiLU of q, k (thread tid < 256 owns one channel)
+    const int c = (tid < HK) ? kh * HK + tid : 2048 + kh * HK + (tid - HK);
+    const float y = conv1(c);
+    if (vh < 16) ring[tw * CONV + c] = x[c];
+    if (tid < HK) {
+      const int cv = 4096 + vh * HK + tid;
+      sm.v[tid] = conv1(cv);
+      ring[tw * CONV + cv] = x[cv];
+      sm.z[tid] = bf2f(x[Z_OFF + vh * HK + tid]);
+    }
+    const float ss = warp_sum(y * y);  // warps 0-3: q, warps 4-7: k
+    if (lane == 0) sm.red[warp] = ss;
+    pconsumer_sync();
+    const float tq = (sm.red[0] + sm.red[1]) + (sm.red[2] + sm.red[3]);
+    const float tk = (sm.red[4] + sm.red[5]) + (sm.red[6] + sm.red[7]);
+    if (tid < HK) sm.q[tid] = y * (1.0f / sqrtf(tq + EPS));
+    else sm.k[tid - HK] = y * (1.0f / sqrtf(tk + EPS));
+    const float biased = bf2f(x[A_OFF + vh]) + a.dt_bias[vh];
+    const float sp = (biased > 20.0f) ? biased : logf(1.0f + expf(biased));
+    const float decay = expf(sp * a.ssm_a[vh]);
+    const float beta = sigmoid_exact(bf2f(x[B_OFF + vh]));
+    pconsumer_sync();
+    const float4 k4 = reinterpret_cast<const float4*>(sm.k)[lane];
+    const float4 q4 = reinterpret_cast<const float4*>(sm.q)[lane];
+
+    // ---- delta rule over the 4 chunks: warp w owns rows 4w..4w+3 of a chunk
+    float ssq = 0.0f;
+    for (int j = 0; j < HK / PCHUNK; ++j, ++i) {
+      const int s = i % PSTAGES;
+      if (!aborted && !mbar_wait(&sm.full[s], (i / PSTAGES) & 1, a.err)) aborted = true;
+      if (aborted) continue;
+      const float4* srow = reinterpret_cast<const float4*>(sm.st[s]);
+      float4 rr[4];
+      float skr[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        float4 v = srow[(warp * 4 + r) * 32 + lane];
+        v.x *= decay; v.y *= decay; v.z *= decay; v.w *= decay;
+        rr[r] = v;
+        float d = v.x * k4.x;
+        d = fmaf(v.y, k4.y, d);
+        d = fmaf(v.z, k4.z, d);
+        d = fmaf(v.w, k4.w, d);
+        skr[r] = d;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.empty[s]);  // stage free: rows are in registers
+#pragma unroll
+      for (int m = 16; m >= 1; m >>= 1)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) skr[r] += __shfl_xor_sync(FULL_MASK, skr[r], m);
+      float o[4];
+      float4* grow = reinterpret_cast<float4*>(st + j * PCHUNK * HK);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int row = warp * 4 + r;
+        const float dd = beta * (sm.v[j * PCHUNK + row] - skr[r]);
+        float4 v = rr[r];
+        v.x = fmaf(k4.x, dd, v.x);
+        v.y = fmaf(k4.y, dd, v.y);
+        v.z = fmaf(k4.z, dd, v.z);
+        v.w = fmaf(k4.w, dd, v.w);
+        __stcs(grow + row * 32 + lane, v);
+        float d = v.x * q4.x;
+        d = fmaf(v.y, q4.y, d);
+        d = fmaf(v.z, q4.z, d);
+        d = fmaf(v.w, q4.w, d);
+        o[r] = d;
+      }
+#pragma unroll
+      for (int m = 16; m >= 1; m >>= 1)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) o[r] += __shfl_xor_sync(FULL_MASK, o[r], m);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float ov = o[r] * SSM_SCALE;
+        if (lane == r) sm.o[j * PCHUNK + warp * 4 + r] = ov;
+        ssq = fmaf(ov, ov, ssq);
+      }
+    }
+    // ---- gated RMSNorm (src/engine.cpp:3307-3322)
+    if (lane == 0) sm.red[PCONSUMERS + warp] = ssq;
+    pconsumer_sync();
+    float tot = 0.0f;
+#pragma unroll
+    for (int q = 0; q < PCONSUMERS; ++q) tot += sm.red[PCONSUMERS + q];
+    if (!aborted && tid < HK) {
+      const float rms = 1.0f / sqrtf(tot / 128.0f + EPS);
+      const float yy = (sm.o[tid] * rms) * a.ssm_norm[tid] * silu_exact(sm.z[tid]);
+      a.out[(int64_t)b * 4096 + vh * HK + tid] = f2bf(yy);
+    }
+    pconsumer_sync();  // sm.q/k/v/z/o/red are rewritten by the next item
+  }
+}
+
+cudaError_t launch_persistent(const GdnArgs& a, cudaStream_t s) {
+  static int configured_device = -1;
+  static int nsm = 148;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(gdn_decode_persistent,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(PSmem));
+    if (e != cudaSuccess) return e;
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    configured_device = dev;
+  }
+  const int items = a.n * 32;
+  const int grid = items < 2 * nsm ? items : 2 * nsm;
+  gdn_decode_persistent<<<grid, PTHREADS, sizeof(PSmem), s>>>(a);
+  return cudaGetLastError();
+}
+
 template <int R, int T>
 cudaError_t launch_r(const GdnArgs& a, cudaStream_t s) {
   constexpr int smem = (HK / R) * HK * 4;
@@ -258,7 +446,7 @@ cudaError_t launch_gdn_decode(const GdnArgs& a, cudaStream_t s) {
   // SMs; large batches give each (sequence, head) one CTA streaming the whole
   // 64 KiB state slice.
   if (a.n <= 8) return launch_r<8, 128>(a, s);
-  return launch_r<1, 256>(a, s);
+  return launch_persistent(a, s);
 }
 
 }  // namespace qc

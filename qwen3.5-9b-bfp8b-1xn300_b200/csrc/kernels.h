@@ -47,10 +47,9 @@ struct AttnArgs {
   float* part_m;             // [slots][4] (log2 domain)
   float* part_l;             // [slots][4]
   float* part_o;             // [slots][4][256]
+  const int32_t* split;      // [2] page-heads in the batch, page-heads per CTA
   int32_t n;
-  int32_t total;             // page-heads in the batch
-  int32_t per;               // page-heads per CTA
-  int32_t grid;              // CTAs
+  int32_t grid;              // CTAs (the SM count; CTAs past the work exit)
   int* err;
 };
 // Combine the partials of each (sequence, kv-head) pair, apply the gate and
@@ -62,8 +61,8 @@ struct CombineArgs {
   const float* part_m;
   const float* part_l;
   const float* part_o;
+  const int32_t* split;
   int32_t n;
-  int32_t per;
 };
 // tmk / tmv: 2D tensor maps over this layer's K / V pool viewed as
 // [max_pages * 4 * 64 rows][256 bf16], box 16 rows x 64 columns, 128 B swizzle.

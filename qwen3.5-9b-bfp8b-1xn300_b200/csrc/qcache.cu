@@ -285,7 +285,8 @@ const char* qc_last_error(const qc_ctx* ctx) { return ctx ? ctx->err.c_str() : g
 int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
   if (!cfg || !out) return QC_ERR_ARG;
   *out = nullptr;
-  if (cfg->n_attn_layers <= 0 || cfg->n_gdn_layers < 0 || cfg->max_seqs <= 0 ||
+  if (cfg->n_attn_layers < 0 || cfg->n_gdn_layers < 0 ||
+      cfg->n_attn_layers + cfg->n_gdn_layers <= 0 || cfg->max_seqs <= 0 ||
       cfg->max_pages <= 0 || cfg->max_ctx <= 0 || cfg->max_batch <= 0 ||
       cfg->max_snapshots < 0 || cfg->max_batch > cfg->max_seqs)
     return QC_ERR_ARG;
@@ -319,7 +320,7 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
   if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
   cudaDeviceGetAttribute(&c->nsm, cudaDevAttrMultiProcessorCount, device);
   const int na = cfg->n_attn_layers, ng = cfg->n_gdn_layers;
-  const int64_t pool = (int64_t)na * cfg->max_pages * PAGE_ELEMS;
+  const int64_t pool = (int64_t)std::max(na, 1) * cfg->max_pages * PAGE_ELEMS;
   c->part_slots = 4 * cfg->max_batch + c->nsm + 8;
   c->job_cap = cfg->max_batch * (1 + 3 * std::max(ng, 1) + 2 * na) + 64;
   struct A { void** p; size_t bytes; const char* what; };
@@ -330,8 +331,8 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
       {(void**)&c->ring, (size_t)cfg->max_seqs * std::max(ng, 1) * RING_ELEMS * 2, "ring"},
       {(void**)&c->snap_state, (size_t)std::max(cfg->max_snapshots, 1) * std::max(ng, 1) * QC_GDN_STATE * 4, "snap_state"},
       {(void**)&c->snap_hist, (size_t)std::max(cfg->max_snapshots, 1) * std::max(ng, 1) * HIST_ELEMS * 2, "snap_hist"},
-      {(void**)&c->q_norm, (size_t)na * HD * 4, "q_norm"},
-      {(void**)&c->k_norm, (size_t)na * HD * 4, "k_norm"},
+      {(void**)&c->q_norm, (size_t)std::max(na, 1) * HD * 4, "q_norm"},
+      {(void**)&c->k_norm, (size_t)std::max(na, 1) * HD * 4, "k_norm"},
       {(void**)&c->ssm_a, (size_t)std::max(ng, 1) * 32 * 4, "ssm_a"},
       {(void**)&c->dt_bias, (size_t)std::max(ng, 1) * 32 * 4, "dt_bias"},
       {(void**)&c->ssm_norm, (size_t)std::max(ng, 1) * 128 * 4, "ssm_norm"},
@@ -339,7 +340,7 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
       {(void**)&c->rope_cos, (size_t)cfg->max_ctx * 32 * 4, "rope_cos"},
       {(void**)&c->rope_sin, (size_t)cfg->max_ctx * 32 * 4, "rope_sin"},
       {(void**)&c->page_table, (size_t)cfg->max_seqs * c->pt_stride * 4, "page_table"},
-      {(void**)&c->desc, (size_t)(5 * cfg->max_batch + 8) * 4, "desc"},
+      {(void**)&c->desc, (size_t)(5 * cfg->max_batch + 8) * 4, "desc"},  // see qc_decode_begin
       {(void**)&c->part_m, (size_t)c->part_slots * 4 * 4, "part_m"},
       {(void**)&c->part_l, (size_t)c->part_slots * 4 * 4, "part_l"},
       {(void**)&c->part_o, (size_t)c->part_slots * 4 * HD * 4, "part_o"},
@@ -661,20 +662,21 @@ int qc_decode_begin(qc_ctx* c, const int32_t* seq_ids, int32_t n, const int32_t*
   }
   c->b_has_tok = tokens != nullptr;
   if (tokens) c->b_tok.assign(tokens, tokens + n);
+  // split-K sizes live in the device descriptor, so that a captured graph of
+  // the layer calls stays valid as the contexts grow; the grid is the SM count
   c->b_total = c->b_seg[n];
-  c->b_grid = std::min(c->b_total, c->nsm);
+  c->b_grid = c->nsm;
   c->b_per = (c->b_total + c->b_grid - 1) / c->b_grid;
-  c->b_grid = (c->b_total + c->b_per - 1) / c->b_per;
   if (!c->host_only) {
     int rc = run_jobs(c, cow, st, nullptr);
     if (rc) return rc;
     if ((rc = sync_rows(c, st))) return rc;
-    const size_t words = 5 * (size_t)n + 1;
+    const size_t words = 5 * (size_t)n + 3;
     char* buf = nullptr;
     int si = 0;
     if ((rc = stage_acquire(c, words * 4, &buf, &si))) return rc;
     int32_t* d = reinterpret_cast<int32_t*>(buf);
-    // layout: slots[n] | pos[n] | seg[n+1] | page0[n] | append[n]
+    // layout: slots[n] | pos[n] | seg[n+1] | page0[n] | append[n] | total, per
     for (int32_t i = 0; i < n; ++i) {
       d[i] = seq_ids[i];
       d[n + i] = c->b_pos[i];
@@ -682,6 +684,8 @@ int qc_decode_begin(qc_ctx* c, const int32_t* seq_ids, int32_t n, const int32_t*
       d[4 * n + 1 + i] = 1;
     }
     for (int32_t i = 0; i <= n; ++i) d[2 * n + i] = c->b_seg[i];
+    d[5 * n + 1] = c->b_total;
+    d[5 * n + 2] = c->b_per;
     QC_CUDA(c, cudaMemcpyAsync(c->desc, buf, words * 4, cudaMemcpyHostToDevice, st));
     if ((rc = stage_release(c, si, st))) return rc;
   }
@@ -715,9 +719,8 @@ int qc_attn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc
   a.part_m = c->part_m;
   a.part_l = c->part_l;
   a.part_o = c->part_o;
+  a.split = c->desc + 5 * n + 1;
   a.n = n;
-  a.total = c->b_total;
-  a.per = c->b_per;
   a.grid = c->b_grid;
   a.err = c->dev_err;
   qc::CombineArgs cb{};
@@ -727,8 +730,8 @@ int qc_attn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc
   cb.part_m = c->part_m;
   cb.part_l = c->part_l;
   cb.part_o = c->part_o;
+  cb.split = a.split;
   cb.n = n;
-  cb.per = c->b_per;
   QC_CUDA(c, qc::launch_attn_decode(a, cb, c->tm_k[layer], c->tm_v[layer], (cudaStream_t)stream));
   return QC_OK;
 }
@@ -766,6 +769,13 @@ int qc_decode_end(qc_ctx* c) {
     if (c->b_has_tok && q.tokens.size() == (size_t)q.len) q.tokens.push_back(c->b_tok[i]);
     q.len += 1;
   }
+  c->in_step = false;
+  return QC_OK;
+}
+
+int qc_decode_abort(qc_ctx* c) {
+  if (!c) return QC_ERR_ARG;
+  if (!c->in_step) return fail(c, QC_ERR_ARG, "no open decode step");
   c->in_step = false;
   return QC_OK;
 }

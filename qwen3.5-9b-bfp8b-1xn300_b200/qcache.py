@@ -88,6 +88,7 @@ def lib() -> C.CDLL:
         "qc_attn_decode": (C.c_int, [P, C.c_int, P, P, P]),
         "qc_gdn_decode": (C.c_int, [P, C.c_int, P, P, P]),
         "qc_decode_end": (C.c_int, [P]),
+        "qc_decode_abort": (C.c_int, [P]),
         "qc_seq_match_prefix": (C.c_int, [P, I32, PI32, I32, PI32, P]),
         "qc_prefix_insert": (C.c_int, [P, I32, PI32, I32, PI32, P]),
         "qc_prefix_lookup": (C.c_int, [P, PI32, I32, PI32, PI32]),
@@ -210,6 +211,9 @@ class QCache:
 
     def decode_end(self):
         self._ck(self.L.qc_decode_end(self.h))
+
+    def decode_abort(self):
+        self._ck(self.L.qc_decode_abort(self.h))
 
     # ---- prefix cache
     def match_prefix(self, s, tokens, stream=0) -> int:
