@@ -482,30 +482,51 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (cur_b >= 0) flush();
 }
 
+// One CTA per (sequence, kv-head pair, head of the group); the slots of the
+// CTAs that covered the pair (at most one per SM, plus one) are weighed in
+// parallel first, so the per-dimension merge below is a chain of independent
+// loads rather than a serial max/sum walk.
 __global__ void __launch_bounds__(256) attn_combine_kernel(const CombineArgs c) {
-  const int pair = blockIdx.x;
+  __shared__ float s_w[512];
+  __shared__ float s_red[8];
+  const int pair = blockIdx.x, hh = blockIdx.y;
   const int b = pair >> 2, kvh = pair & 3, t = threadIdx.x;
   const int np = (c.seg[b + 1] - c.seg[b]) >> 2;
   const int u0 = c.seg[b] + kvh * np;
   const int per = c.split[1];
-  const int c0 = u0 / per, c1 = (u0 + np - 1) / per;
-  const uint16_t* prow = c.proj + (int64_t)b * 10240;
+  const int c0 = u0 / per, ns = (u0 + np - 1) / per - c0 + 1;
+  const int base = pair + c0;
+  // max over the slots
+  float m = -INFINITY;
+  for (int k = t; k < ns; k += 256) m = fmaxf(m, c.part_m[(base + k) * 4 + hh]);
+  m = warp_max(m);
+  if ((t & 31) == 0) s_red[t >> 5] = m;
+  __syncthreads();
+  float M = s_red[0];
 #pragma unroll
-  for (int hh = 0; hh < 4; ++hh) {
-    float M = -INFINITY;
-    for (int k = c0; k <= c1; ++k) M = fmaxf(M, c.part_m[(pair + k) * 4 + hh]);
-    float O = 0.0f, L = 0.0f;
-    for (int k = c0; k <= c1; ++k) {
-      const int sl = pair + k;
-      const float mk = c.part_m[sl * 4 + hh];
-      const float f = (mk == -INFINITY) ? 0.0f : exp2f(mk - M);
-      L = fmaf(f, c.part_l[sl * 4 + hh], L);
-      O = fmaf(f, c.part_o[((int64_t)sl * 4 + hh) * HD + t], O);
-    }
-    const int h = kvh * 4 + hh;
-    const float g = bf2f(prow[h * 2 * HD + HD + t]);
-    c.out[(int64_t)b * 4096 + h * HD + t] = f2bf((O / L) * sigmoid_exact(g));
+  for (int w = 1; w < 8; ++w) M = fmaxf(M, s_red[w]);
+  __syncthreads();
+  // slot weights and the softmax sum
+  float l = 0.0f;
+  for (int k = t; k < ns; k += 256) {
+    const float mk = c.part_m[(base + k) * 4 + hh];
+    const float f = (mk == -INFINITY) ? 0.0f : exp2f(mk - M);
+    s_w[k] = f;
+    l = fmaf(f, c.part_l[(base + k) * 4 + hh], l);
   }
+  l = warp_sum(l);
+  if ((t & 31) == 0) s_red[t >> 5] = l;
+  __syncthreads();
+  float L = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) L += s_red[w];
+  float O = 0.0f;
+  const float* po = c.part_o + ((int64_t)base * 4 + hh) * HD + t;
+#pragma unroll 8
+  for (int k = 0; k < ns; ++k) O = fmaf(s_w[k], po[(int64_t)k * 4 * HD], O);
+  const int h = kvh * 4 + hh;
+  const float g = bf2f(c.proj[(int64_t)b * 10240 + h * 2 * HD + HD + t]);
+  c.out[(int64_t)b * 4096 + h * HD + t] = f2bf((O / L) * sigmoid_exact(g));
 }
 
 }  // namespace
@@ -528,7 +549,7 @@ cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CU
   attn_partial_kernel<<<a.grid, THREADS, attn_smem_bytes(), s>>>(a, tmk, tmv);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  attn_combine_kernel<<<c.n * 4, 256, 0, s>>>(c);
+  attn_combine_kernel<<<dim3(c.n * 4, 4), 256, 0, s>>>(c);
   return cudaGetLastError();
 }
 
