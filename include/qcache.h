@@ -209,6 +209,36 @@ int qc_attn_partial(qc_ctx* ctx, int attn_layer, const uint16_t* proj_dev, int32
 int qc_attn_combine(qc_ctx* ctx, const float* partials_dev, int32_t n_parts,
                     const uint16_t* proj_dev, uint16_t* out_dev, qc_stream stream);
 
+/* ------------------------------------------- decode without device allocation */
+
+/* No counterpart in the reference.  For callers that may not allocate device
+ * memory (an engine that owns all GPU memory in its own arena, a plugin
+ * running inside another framework's pool, a process capped at a fixed
+ * footprint): one full-attention decode step like qc_attn_decode, but with no
+ * context and no allocation.  The caller passes everything that persists:
+ *   k_pool_dev, v_pool_dev [max_pages][4][64][256] bf16 (one layer);
+ *   page_table_dev [n][pt_stride] int32, row i mapping sequence i's pages;
+ *   pos (host) [n]: position of each sequence's new token, whose K/V are
+ *     appended into its page; q_norm_dev, k_norm_dev [256] f32;
+ *   rope_cos_dev, rope_sin_dev [>= max(pos) + 1][32] f32, the table of
+ *     precompute_rope (src/engine.cpp:2408-2420);
+ *   proj_dev [n][10240] and out_dev [n][4096] bf16.
+ * The kernels' scratch (split-K partial records, step descriptor) is one
+ * fixed array of about 1.9 MB compiled into the library, resident on every GPU
+ * that loads it until exit.  Limits: n <= QC_NOALLOC_MAX_BATCH and at most
+ * QC_NOALLOC_MAX_CTAS SMs; larger requests return QC_ERR_ARG.  All calls on a
+ * device share that array: calls that overlap on the GPU race, so serialise
+ * them.  The first call on each device looks up the array's address with that
+ * device current; make it before any stream capture.  On failure
+ * qc_last_error(NULL) describes the error. */
+#define QC_NOALLOC_MAX_BATCH 64
+#define QC_NOALLOC_MAX_CTAS  192
+int qc_attn_decode_noalloc(const uint16_t* proj_dev, uint16_t* k_pool_dev, uint16_t* v_pool_dev,
+                           int32_t max_pages, const int32_t* page_table_dev, int32_t pt_stride,
+                           const int32_t* pos, int32_t n, const float* q_norm_dev,
+                           const float* k_norm_dev, const float* rope_cos_dev,
+                           const float* rope_sin_dev, uint16_t* out_dev, qc_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

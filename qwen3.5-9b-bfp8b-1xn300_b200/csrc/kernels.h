@@ -70,6 +70,9 @@ cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CU
                                const CUtensorMap& tmv, cudaStream_t s);
 int attn_smem_bytes();
 
+// Message returned by qc_last_error(NULL) on this thread (qcache.cu).
+void set_thread_error(const char* msg);
+
 // Copies (kv_copy.cu).
 // Scatter / gather of positions [pos0, pos0 + n) of one sequence between a
 // contiguous [n][4][256] array and the paged pool of one layer.

@@ -282,6 +282,12 @@ static thread_local std::string g_create_err;
 
 const char* qc_last_error(const qc_ctx* ctx) { return ctx ? ctx->err.c_str() : g_create_err.c_str(); }
 
+}  // extern "C"
+
+void qc::set_thread_error(const char* msg) { g_create_err = msg; }
+
+extern "C" {
+
 int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
   if (!cfg || !out) return QC_ERR_ARG;
   *out = nullptr;

@@ -98,6 +98,7 @@ def lib() -> C.CDLL:
         "qc_prefix_page_hashes": (C.c_int, [PI32, I32, C.POINTER(C.c_uint64)]),
         "qc_attn_partial": (C.c_int, [P, C.c_int, P, I32, I32, I32, P, P]),
         "qc_attn_combine": (C.c_int, [P, P, I32, P, P, P]),
+        "qc_attn_decode_noalloc": (C.c_int, [P, P, P, I32, P, I32, PI32, I32, P, P, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -262,3 +263,16 @@ def page_hashes(tokens) -> list[int]:
     if rc:
         raise QCacheError(rc, "qc_prefix_page_hashes")
     return list(out[: n // PAGE])
+
+
+def attn_decode_noalloc(proj_ptr, k_pool_ptr, v_pool_ptr, max_pages, page_table_ptr, pt_stride,
+                        pos, q_norm_ptr, k_norm_ptr, rope_cos_ptr, rope_sin_ptr, out_ptr,
+                        stream=0):
+    """qc_attn_decode_noalloc: attention decode over caller-owned buffers, with
+    no device allocation (see include/qcache.h)."""
+    L = lib()
+    rc = L.qc_attn_decode_noalloc(proj_ptr, k_pool_ptr, v_pool_ptr, max_pages, page_table_ptr,
+                                  pt_stride, _i32arr(pos), len(pos), q_norm_ptr, k_norm_ptr,
+                                  rope_cos_ptr, rope_sin_ptr, out_ptr, stream)
+    if rc:
+        raise QCacheError(rc, L.qc_last_error(None).decode())
