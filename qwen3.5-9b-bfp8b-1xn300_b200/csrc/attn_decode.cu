@@ -41,7 +41,10 @@ namespace {
 
 constexpr int HD = 256;
 constexpr int PAGE = 64;
-constexpr int STAGES = 3;
+#ifndef QC_ATTN_STAGES
+#define QC_ATTN_STAGES 3
+#endif
+constexpr int STAGES = QC_ATTN_STAGES;
 constexpr int N_CONSUMER = 8;
 constexpr int THREADS = (N_CONSUMER + 1) * 32;
 constexpr int TILE_ELEMS = PAGE * HD;     // one K or V page-head, 32 KiB
