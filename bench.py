@@ -44,6 +44,18 @@ GDN_BYTES_PER_SEQ = (2 * 32 * 128 * 128 * 4      # state read + write
 GDN_BYTES_PER_LAUNCH = 4 * 8192 * 4 + 32 * 4 * 2 + 128 * 4   # conv weights + small params
 
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
+# the dominant kernel, per sequence, from the ncu captures summarised in
+# profiles/ (captured on smaller cases, scaled by the sequences processed):
+PROFILED_TRAFFIC_PER_SEQ = {
+    "stack": ("attn", (269.878784e6 + 4.500992e6) / 16,
+              "profiles/attn_partial_stack16.md (16 sequences, scaled)"),
+    "long": ("attn", 537.116672e6 + 5.645312e6, "profiles/attn_partial_long131072.md"),
+    "gdn": ("gdn", (139.216640e6 + 77.228800e6) / 64,
+            "profiles/gdn_decode_persistent_batch64.md (writes partly still in L2)"),
+}
+
+
 def attn_bytes_per_seq(pos: int) -> int:
     # K and V of the pos cached positions, the appended row, proj in, out
     return 4096 * pos + 4096 + 10240 * 2 + 4096 * 2
@@ -349,6 +361,91 @@ def run_ours(args, rank, world, dist, kinds, n_total, ctx):
                 else "inputs larger than L2 (126 MB) on every step")
 
 
+def run_long_split(args, rank, world, dist, n_layers, ctx):
+    """Config 4 over several GPUs: one sequence, split-K over KV pages.  Every
+    rank maps the whole context (and holds the KV of all pages, so any range is
+    valid); rank r attends pages [cut_r, cut_{r+1}) and the last rank also the
+    new token (it owns the growing tail).  Per layer: qc_attn_partial -> NCCL
+    all-gather of the [16][258] f32 records -> qc_attn_combine on every rank."""
+    import torch
+    qc = load_pkg("qcache")
+    synth = load_pkg("synth")
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    stream = torch.cuda.current_stream().cuda_stream
+    kinds = ["a"] * n_layers
+    stack = Stack(qc, synth, torch, kinds, 1, ctx, args.warmup + args.steps + 8, seed=1000,
+                  stream=stream)
+    q = stack.q
+    pages0 = ctx // 64 + 1
+    cuts = [r * pages0 // world for r in range(world)] + [None]
+    recs = torch.zeros(n_layers, 16, 258, device="cuda")
+    gathered = torch.zeros(n_layers, world, 16, 258, device="cuda")
+
+    def begin():
+        q.decode_begin(stack.seqs, stream=stream)
+        pos = q.seq_len(stack.seqs[0])
+        pe = cuts[rank + 1] if rank + 1 < world else pos // 64 + 1
+        q.attn_partial_range(cuts[rank], pe, int(rank == world - 1), stream)
+
+    def layers(st):
+        for l in range(n_layers):
+            q.attn_partial(l, stack.proj[l].data_ptr(), recs[l].data_ptr(), st)
+            dist.all_gather_into_tensor(gathered[l], recs[l])
+            q.attn_combine(gathered[l].data_ptr(), world, stack.proj[l].data_ptr(),
+                           stack.out[l].data_ptr(), st)
+
+    # one step captured into a CUDA graph (partials, NCCL all-gathers and
+    # merges); the range descriptor is uploaded per step outside the graph
+    begin()
+    layers(stream)            # warm: NCCL communicator set up before capture
+    q.decode_end()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    begin()
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph):
+        layers(torch.cuda.current_stream().cuda_stream)
+    q.decode_abort()
+    torch.cuda.synchronize()
+
+    def step():
+        begin()
+        graph.replay()
+        q.decode_end()
+
+    for _ in range(args.warmup):
+        step()
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.5)
+    attn_b = 0
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(args.steps):
+        attn_b += attn_bytes_per_seq(q.seq_len(stack.seqs[0]))
+        step()
+    t1.record()
+    dist.barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    q.check_device()
+    vals = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms = vals.item()
+    return dict(ms=ms, e2e_ms=None, attn_ms=ms, gdn_ms=0.0,
+                attn_layer_bytes=attn_b / args.steps / world, gdn_layer_bytes=0.0, n_local=1,
+                h2d=0, d2h=0, clocks=clk, l2="inputs larger than L2 on every step",
+                collective="NCCL all-gather of the (m, l, o) records, one per layer, "
+                           "captured with the kernels in a CUDA graph")
+
+
 # ------------------------------------------------------------ CPU baseline
 
 
@@ -464,7 +561,12 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         dist_mod.init_process_group("nccl")
         dist = dist_mod
-    r = run_ours(args, rank, world, dist, kinds, n_total, ctx)
+    if args.config == "long" and world > 1:
+        r = run_long_split(args, rank, world, dist, len(kinds), ctx)
+        config["sharding"] = f"split-K over KV pages across {world} GPUs"
+        config["collective"] = r["collective"]
+    else:
+        r = run_ours(args, rank, world, dist, kinds, n_total, ctx)
     if dist is not None:
         dist.barrier()
     if rank != 0:
@@ -487,6 +589,11 @@ def main():
         kname, kbytes, kms = ("gdn_decode (one DeltaNet layer)", r["gdn_layer_bytes"],
                               r["gdn_ms"] / n_gdn)
     k_gbs = kbytes / (kms * 1e-3) / 1e9
+    traffic, traffic_src = None, None
+    prof = PROFILED_TRAFFIC_PER_SEQ.get(args.config)
+    kind_now = "attn" if r["attn_ms"] >= r["gdn_ms"] else "gdn"
+    if prof and prof[0] == kind_now and world == 1:
+        traffic, traffic_src = int(prof[1] * r["n_local"]), prof[2]
     line = {
         "metric": metric, "value": round(us, 4), "unit": "us", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 4),
@@ -499,9 +606,12 @@ def main():
                           "deltanet_total": round(r["gdn_ms"], 4)},
         "roofline": {"kernel": kname, "bound": "hbm", "achieved": round(k_gbs, 1),
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                     "frac": round(k_gbs / peak, 4), "traffic": None},
-        "e2e": {"value": round(r["e2e_ms"] * 1e3 / units, 4), "unit": "us",
-                "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+                     "frac": round(k_gbs / peak, 4), "traffic": traffic,
+                     "traffic_source": traffic_src,
+                     "algorithmic_bytes_per_launch": int(kbytes)},
+        "e2e": ({"value": round(r["e2e_ms"] * 1e3 / units, 4), "unit": "us",
+                 "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]}
+                if r["e2e_ms"] is not None else None),
         "gpu_launches": args.steps * (n_gdn + 2 * n_attn),
         "clocks": r["clocks"],
     }

@@ -198,14 +198,23 @@ int qc_prefix_page_hashes(const int32_t* tokens, int32_t n, uint64_t* hashes);
 
 /* --------------------------------------------- split-K across GPUs (long ctx) */
 
-/* Partial attention of the current decode batch's sequence 0 over the KV
- * pages [page_begin, page_end) that this context maps (positions outside the
- * range are not read).  Writes per q-head m (running max, log2 domain),
- * l (sum) and o[256] (unnormalised) as partial_dev [16][2 + 256] f32.  The
- * context that owns the page of the new position appends the token (append
- * != 0).  qc_attn_combine merges G such partials and applies the gate. */
-int qc_attn_partial(qc_ctx* ctx, int attn_layer, const uint16_t* proj_dev, int32_t page_begin,
-                    int32_t page_end, int32_t append, float* partial_dev, qc_stream stream);
+/* Long-context decode of one sequence split over devices by KV position.
+ * Each device's context maps the whole sequence and holds the KV of its page
+ * range.  After qc_decode_begin (batch of one sequence):
+ *   qc_attn_partial_range: this device attends pages [page_begin, page_end);
+ *     append != 0 on the device whose range holds the new position (it
+ *     appends the token and attends to it).  Uploads the step's descriptor.
+ *   qc_attn_partial: per layer, writes the range's record partial_dev
+ *     [16][2 + 256] f32: per q-head m (max of score * log2 e), l (sum of
+ *     2^(s - m)) and o[256] (unnormalised).  Reads the range from device
+ *     memory, so a CUDA graph of the per-layer calls replays for every step.
+ *   qc_attn_combine: merges n_parts records [n_parts][16][258] (all-gathered
+ *     from the devices, e.g. over NCCL) and applies the sigmoid gate:
+ *     out_dev [4096] bf16, as qc_attn_decode would produce. */
+int qc_attn_partial_range(qc_ctx* ctx, int32_t page_begin, int32_t page_end, int32_t append,
+                          qc_stream stream);
+int qc_attn_partial(qc_ctx* ctx, int attn_layer, const uint16_t* proj_dev, float* partial_dev,
+                    qc_stream stream);
 int qc_attn_combine(qc_ctx* ctx, const float* partials_dev, int32_t n_parts,
                     const uint16_t* proj_dev, uint16_t* out_dev, qc_stream stream);
 

@@ -497,6 +497,12 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const CombineArgs c) 
   const int np = (c.seg[b + 1] - c.seg[b]) >> 2;
   const int u0 = c.seg[b] + kvh * np;
   const int per = c.split[1];
+  if (np == 0) {  // empty page range (split over devices): an empty record
+    float* rec = c.record + (kvh * 4 + hh) * (HD + 2);
+    if (t == 0) { rec[0] = -INFINITY; rec[1] = 0.0f; }
+    rec[2 + t] = 0.0f;
+    return;
+  }
   const int c0 = u0 / per, ns = (u0 + np - 1) / per - c0 + 1;
   const int base = pair + c0;
   // max over the slots
@@ -528,11 +534,41 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const CombineArgs c) 
 #pragma unroll 8
   for (int k = 0; k < ns; ++k) O = fmaf(s_w[k], po[(int64_t)k * 4 * HD], O);
   const int h = kvh * 4 + hh;
+  if (c.record) {  // partial of a split over devices: keep it unnormalised
+    float* rec = c.record + h * (HD + 2);
+    if (t == 0) { rec[0] = M; rec[1] = L; }
+    rec[2 + t] = O;
+    return;
+  }
   const float g = bf2f(c.proj[(int64_t)b * 10240 + h * 2 * HD + HD + t]);
   c.out[(int64_t)b * 4096 + h * HD + t] = f2bf((O / L) * sigmoid_exact(g));
 }
 
+// Cross-device merge: one CTA per head, thread = dimension.
+__global__ void __launch_bounds__(256) attn_merge_records_kernel(const float* rec, int n_parts,
+                                                                 const uint16_t* proj,
+                                                                 uint16_t* out) {
+  const int h = blockIdx.x, t = threadIdx.x;
+  float M = -INFINITY;
+  for (int g = 0; g < n_parts; ++g) M = fmaxf(M, rec[(g * 16 + h) * (HD + 2)]);
+  float L = 0.0f, O = 0.0f;
+  for (int g = 0; g < n_parts; ++g) {
+    const float* r = rec + (g * 16 + h) * (HD + 2);
+    const float f = (r[0] == -INFINITY) ? 0.0f : exp2f(r[0] - M);
+    L = fmaf(f, r[1], L);
+    O = fmaf(f, r[2 + t], O);
+  }
+  const float gt = bf2f(proj[h * 2 * HD + HD + t]);
+  out[h * HD + t] = f2bf((O / L) * sigmoid_exact(gt));
+}
+
 }  // namespace
+
+cudaError_t launch_attn_merge_records(const float* records, int32_t n_parts, const uint16_t* proj,
+                                      uint16_t* out, cudaStream_t s) {
+  attn_merge_records_kernel<<<16, 256, 0, s>>>(records, n_parts, proj, out);
+  return cudaGetLastError();
+}
 
 int attn_smem_bytes() { return static_cast<int>(sizeof(Smem)) + 1024; }
 

@@ -63,12 +63,19 @@ struct CombineArgs {
   const float* part_o;
   const int32_t* split;
   int32_t n;
+  // when non-null: write the merged record (m, l, o unnormalised) of sequence
+  // 0 as [16 heads][2 + 256] instead of the gated bf16 output
+  float* record;
 };
 // tmk / tmv: 2D tensor maps over this layer's K / V pool viewed as
 // [max_pages * 4 * 64 rows][256 bf16], box 16 rows x 64 columns, 128 B swizzle.
 cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CUtensorMap& tmk,
                                const CUtensorMap& tmv, cudaStream_t s);
 int attn_smem_bytes();
+// Merge n_parts records [n_parts][16][258] (m, l, o) into the gated bf16
+// output [4096] of one sequence (attn_decode.cu).
+cudaError_t launch_attn_merge_records(const float* records, int32_t n_parts, const uint16_t* proj,
+                                      uint16_t* out, cudaStream_t s);
 
 // Message returned by qc_last_error(NULL) on this thread (qcache.cu).
 void set_thread_error(const char* msg);

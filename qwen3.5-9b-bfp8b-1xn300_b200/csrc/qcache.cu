@@ -80,6 +80,7 @@ struct qc_ctx {
   float* rope_sin = nullptr;
   int32_t* page_table = nullptr;// [max_seqs][pt_stride]
   int32_t* desc = nullptr;      // batch: slots | pos | seg | page0 | append
+  int32_t* desc_part = nullptr; // same layout, one sequence, for qc_attn_partial
   float* part_m = nullptr;
   float* part_l = nullptr;
   float* part_o = nullptr;
@@ -346,7 +347,8 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
       {(void**)&c->rope_cos, (size_t)cfg->max_ctx * 32 * 4, "rope_cos"},
       {(void**)&c->rope_sin, (size_t)cfg->max_ctx * 32 * 4, "rope_sin"},
       {(void**)&c->page_table, (size_t)cfg->max_seqs * c->pt_stride * 4, "page_table"},
-      {(void**)&c->desc, (size_t)(5 * cfg->max_batch + 8) * 4, "desc"},  // see qc_decode_begin
+      {(void**)&c->desc, (size_t)(5 * cfg->max_batch + 8) * 4, "desc"},
+      {(void**)&c->desc_part, 16 * 4, "desc_part"},  // see qc_decode_begin
       {(void**)&c->part_m, (size_t)c->part_slots * 4 * 4, "part_m"},
       {(void**)&c->part_l, (size_t)c->part_slots * 4 * 4, "part_l"},
       {(void**)&c->part_o, (size_t)c->part_slots * 4 * HD * 4, "part_o"},
@@ -424,7 +426,8 @@ void qc_destroy(qc_ctx* c) {
     cudaDeviceSynchronize();
     void* ptrs[] = {c->k_pool, c->v_pool, c->state, c->ring, c->snap_state, c->snap_hist,
                     c->q_norm, c->k_norm, c->ssm_a, c->dt_bias, c->ssm_norm, c->conv_w,
-                    c->rope_cos, c->rope_sin, c->page_table, c->desc, c->part_m, c->part_l,
+                    c->rope_cos, c->rope_sin, c->page_table, c->desc, c->desc_part,
+                    c->part_m, c->part_l,
                     c->part_o, c->jobs, c->chunk_start, c->dev_err};
     for (void* p : ptrs)
       if (p) cudaFree(p);
@@ -990,17 +993,91 @@ int qc_prefix_last_restore_bytes(const qc_ctx* c, int64_t* bytes) {
 
 // ------------------------------------------------- split-K across devices
 
-int qc_attn_partial(qc_ctx* c, int layer, const uint16_t* proj, int32_t page_begin,
-                    int32_t page_end, int32_t append, float* partial, qc_stream stream) {
-  (void)layer; (void)proj; (void)page_begin; (void)page_end; (void)append; (void)partial;
-  (void)stream;
-  return fail(c, QC_ERR_ARG, "qc_attn_partial: not built yet");
+int qc_attn_partial_range(qc_ctx* c, int32_t page_begin, int32_t page_end, int32_t append,
+                          qc_stream stream) {
+  if (!c) return QC_ERR_ARG;
+  if (!c->in_step) return fail(c, QC_ERR_ARG, "no open decode step");
+  if (c->b_seq.size() != 1) return fail(c, QC_ERR_ARG, "split-K needs a batch of 1");
+  QC_NEED_DEVICE(c);
+  const int32_t s = c->b_seq[0], pos = c->b_pos[0];
+  const Seq& q = c->seqs[s];
+  if (page_begin < 0 || page_end < page_begin || page_end > (int32_t)q.pages.size())
+    return fail(c, QC_ERR_ARG, "page range [%d, %d) outside the %zu mapped pages", page_begin,
+                page_end, q.pages.size());
+  const int32_t pos_page = pos / PAGE;
+  if (append && (pos_page < page_begin || pos_page >= page_end))
+    return fail(c, QC_ERR_ARG, "append requested but page %d of position %d is outside [%d, %d)",
+                pos_page, pos, page_begin, page_end);
+  if (!append && page_end > pos_page + (pos % PAGE ? 1 : 0))
+    return fail(c, QC_ERR_ARG, "range [%d, %d) reaches past the cached positions (< %d)",
+                page_begin, page_end, pos);
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = sync_rows(c, st);
+  if (rc) return rc;
+  const int32_t total = 4 * (page_end - page_begin);
+  const int32_t per = std::max(1, (total + c->nsm - 1) / c->nsm);
+  // one-sequence descriptor: slot | pos | seg[2] | page0 | append | total, per
+  int32_t d[8] = {s, pos, 0, total, page_begin, append ? 1 : 0, total, per};
+  char* buf = nullptr;
+  int si = 0;
+  if ((rc = stage_acquire(c, sizeof(d), &buf, &si))) return rc;
+  std::memcpy(buf, d, sizeof(d));
+  QC_CUDA(c, cudaMemcpyAsync(c->desc_part, buf, sizeof(d), cudaMemcpyHostToDevice, st));
+  return stage_release(c, si, st);
+}
+
+int qc_attn_partial(qc_ctx* c, int layer, const uint16_t* proj, float* partial,
+                    qc_stream stream) {
+  if (!c || !proj || !partial) return QC_ERR_ARG;
+  if (!c->in_step) return fail(c, QC_ERR_ARG, "no open decode step");
+  if (c->b_seq.size() != 1) return fail(c, QC_ERR_ARG, "split-K needs a batch of 1");
+  if (layer < 0 || layer >= c->cfg.n_attn_layers) return fail(c, QC_ERR_ARG, "attn layer %d", layer);
+  QC_NEED_DEVICE(c);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t base = (int64_t)layer * c->cfg.max_pages * PAGE_ELEMS;
+  qc::AttnArgs a{};
+  a.proj = proj;
+  a.k_pool = c->k_pool + base;
+  a.v_pool = c->v_pool + base;
+  a.page_table = c->page_table;
+  a.pt_stride = c->pt_stride;
+  a.max_pages = c->cfg.max_pages;
+  a.slots = c->desc_part;
+  a.pos = c->desc_part + 1;
+  a.seg = c->desc_part + 2;
+  a.page0 = c->desc_part + 4;
+  a.append = c->desc_part + 5;
+  a.split = c->desc_part + 6;
+  a.q_norm = c->q_norm + layer * HD;
+  a.k_norm = c->k_norm + layer * HD;
+  a.rope_cos = c->rope_cos;
+  a.rope_sin = c->rope_sin;
+  a.part_m = c->part_m;
+  a.part_l = c->part_l;
+  a.part_o = c->part_o;
+  a.n = 1;
+  a.grid = c->nsm;
+  a.err = c->dev_err;
+  qc::CombineArgs cb{};
+  cb.proj = proj;
+  cb.out = nullptr;
+  cb.seg = a.seg;
+  cb.part_m = c->part_m;
+  cb.part_l = c->part_l;
+  cb.part_o = c->part_o;
+  cb.split = a.split;
+  cb.n = 1;
+  cb.record = partial;
+  QC_CUDA(c, qc::launch_attn_decode(a, cb, c->tm_k[layer], c->tm_v[layer], st));
+  return QC_OK;
 }
 
 int qc_attn_combine(qc_ctx* c, const float* partials, int32_t n_parts, const uint16_t* proj,
                     uint16_t* out, qc_stream stream) {
-  (void)partials; (void)n_parts; (void)proj; (void)out; (void)stream;
-  return fail(c, QC_ERR_ARG, "qc_attn_combine: not built yet");
+  if (!c || !partials || !proj || !out || n_parts <= 0) return QC_ERR_ARG;
+  QC_NEED_DEVICE(c);
+  QC_CUDA(c, qc::launch_attn_merge_records(partials, n_parts, proj, out, (cudaStream_t)stream));
+  return QC_OK;
 }
 
 }  // extern "C"

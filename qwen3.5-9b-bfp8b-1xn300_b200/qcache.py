@@ -96,7 +96,8 @@ def lib() -> C.CDLL:
         "qc_prefix_release": (C.c_int, [P, I32]),
         "qc_prefix_last_restore_bytes": (C.c_int, [P, C.POINTER(C.c_int64)]),
         "qc_prefix_page_hashes": (C.c_int, [PI32, I32, C.POINTER(C.c_uint64)]),
-        "qc_attn_partial": (C.c_int, [P, C.c_int, P, I32, I32, I32, P, P]),
+        "qc_attn_partial_range": (C.c_int, [P, I32, I32, I32, P]),
+        "qc_attn_partial": (C.c_int, [P, C.c_int, P, P, P]),
         "qc_attn_combine": (C.c_int, [P, P, I32, P, P, P]),
         "qc_attn_decode_noalloc": (C.c_int, [P, P, P, I32, P, I32, PI32, I32, P, P, P, P, P, P]),
     }
@@ -248,9 +249,11 @@ class QCache:
         return b.value
 
     # ---- split-K across devices
-    def attn_partial(self, layer, proj_ptr, page_begin, page_end, append, partial_ptr, stream=0):
-        self._ck(self.L.qc_attn_partial(self.h, layer, proj_ptr, page_begin, page_end, append,
-                                        partial_ptr, stream))
+    def attn_partial_range(self, page_begin, page_end, append, stream=0):
+        self._ck(self.L.qc_attn_partial_range(self.h, page_begin, page_end, append, stream))
+
+    def attn_partial(self, layer, proj_ptr, partial_ptr, stream=0):
+        self._ck(self.L.qc_attn_partial(self.h, layer, proj_ptr, partial_ptr, stream))
 
     def attn_combine(self, partials_ptr, n_parts, proj_ptr, out_ptr, stream=0):
         self._ck(self.L.qc_attn_combine(self.h, partials_ptr, n_parts, proj_ptr, out_ptr, stream))
