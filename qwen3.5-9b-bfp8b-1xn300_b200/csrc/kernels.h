@@ -96,8 +96,9 @@ struct CopyJob {
   void* dst;
   int64_t bytes;
 };
+// Chunks run through the bulk-copy engine: addresses and sizes multiples of 16.
 cudaError_t launch_copy_jobs(const CopyJob* jobs_dev, int32_t n_jobs, const int64_t* chunk_start_dev,
-                             int64_t n_chunks, int32_t chunk, cudaStream_t s);
+                             int64_t n_chunks, int32_t chunk, int* err, cudaStream_t s);
 // Conv ring <-> oldest-first [3][8192] history of one layer of one sequence.
 cudaError_t launch_ring_to_hist(const uint16_t* ring, int32_t pos, uint16_t* hist, cudaStream_t s);
 cudaError_t launch_hist_to_ring(const uint16_t* hist, int32_t pos, uint16_t* ring, cudaStream_t s);

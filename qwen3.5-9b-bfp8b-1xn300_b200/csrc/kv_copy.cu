@@ -47,37 +47,82 @@ __global__ void __launch_bounds__(128) kv_gather_kernel(const uint16_t* k_pool,
   *reinterpret_cast<uint4*>(v + dst) = *reinterpret_cast<const uint4*>(v_pool + src);
 }
 
-// Grid-stride over chunks; chunk c belongs to the job j with
-// chunk_start[j] <= c < chunk_start[j + 1].  Each thread moves 4 x 16 B per
-// iteration with all four loads issued before the stores.
-__global__ void __launch_bounds__(256) copy_jobs_kernel(const CopyJob* jobs, int32_t n_jobs,
-                                                        const int64_t* chunk_start,
-                                                        int64_t n_chunks, int32_t chunk) {
-  for (int64_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
-    int lo = 0, hi = n_jobs - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (chunk_start[mid] <= c) lo = mid; else hi = mid - 1;
-    }
-    const CopyJob jb = jobs[lo];
-    const int64_t off = (c - chunk_start[lo]) * chunk;
-    const int64_t bytes = min((int64_t)chunk, jb.bytes - off);
-    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const char*>(jb.src) + off);
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<char*>(jb.dst) + off);
-    const int n16 = static_cast<int>(bytes >> 4);
-    int k = threadIdx.x;
-    for (; k + 3 * 256 < n16; k += 4 * 256) {
-      const uint4 a0 = __ldcs(src + k);
-      const uint4 a1 = __ldcs(src + k + 256);
-      const uint4 a2 = __ldcs(src + k + 512);
-      const uint4 a3 = __ldcs(src + k + 768);
-      __stcs(dst + k, a0);
-      __stcs(dst + k + 256, a1);
-      __stcs(dst + k + 512, a2);
-      __stcs(dst + k + 768, a3);
-    }
-    for (; k < n16; k += 256) __stcs(dst + k, __ldcs(src + k));
+// Batched copy jobs; chunk c belongs to the job j with chunk_start[j] <= c <
+// chunk_start[j + 1].  One thread per CTA drives the bulk-copy engine.  The
+// CTA's chunks (a contiguous range) stream global -> shared memory
+// (cp.async.bulk, completing on an mbarrier) -> global (cp.async.bulk store,
+// bulk groups) through a BULK_STAGES-deep ring of `chunk`-byte buffers, so
+// BULK_STAGES loads are in flight per SM with no per-byte instructions.
+#ifndef QC_BULK_STAGES
+#define QC_BULK_STAGES 2
+#endif
+#ifndef QC_BULK_CTAS
+#define QC_BULK_CTAS 4
+#endif
+constexpr int BULK_STAGES = QC_BULK_STAGES;
+
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(32) copy_jobs_bulk_kernel(const CopyJob* jobs, int32_t n_jobs,
+                                                            const int64_t* chunk_start,
+                                                            int64_t n_chunks, int32_t chunk,
+                                                            int* err) {
+  extern __shared__ __align__(128) unsigned char stage[];
+  __shared__ __align__(8) uint64_t full[BULK_STAGES];
+  if (threadIdx.x != 0) return;
+  for (int i = 0; i < BULK_STAGES; ++i) mbar_init(&full[i], 1);
+  fence_mbar_init();
+  // contiguous chunk range of this CTA; a job cursor that only moves forward
+  const int64_t per = (n_chunks + gridDim.x - 1) / gridDim.x;
+  const int64_t c_begin = blockIdx.x * per;
+  const int64_t K = max((int64_t)0, min(n_chunks, c_begin + per) - c_begin);
+  int lo = 0, hi = n_jobs - 1;  // job of the first chunk
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (chunk_start[mid] <= c_begin) lo = mid; else hi = mid - 1;
   }
+  int cur = lo;
+  CopyJob jb = jobs[cur];
+  int64_t next_start = chunk_start[cur + 1];
+  auto resolve = [&](int64_t k, const char*& src, char*& dst, uint32_t& bytes) {
+    const int64_t c = c_begin + k;  // called with non-decreasing k
+    while (c >= next_start) {
+      ++cur;
+      jb = jobs[cur];
+      next_start = chunk_start[cur + 1];
+    }
+    const int64_t off = (c - chunk_start[cur]) * chunk;
+    bytes = static_cast<uint32_t>(min((int64_t)chunk, jb.bytes - off));
+    src = static_cast<const char*>(jb.src) + off;
+    dst = static_cast<char*>(jb.dst) + off;
+  };
+  char* dst_of[BULK_STAGES];
+  uint32_t bytes_of[BULK_STAGES];
+  auto load = [&](int64_t k) {
+    const char* src;
+    const int s = static_cast<int>(k % BULK_STAGES);
+    resolve(k, src, dst_of[s], bytes_of[s]);
+    mbar_arrive_expect_tx(&full[s], bytes_of[s]);
+    bulk_g2s(stage + (size_t)s * chunk, src, bytes_of[s], &full[s]);
+  };
+  for (int64_t k = 0; k < K && k < BULK_STAGES; ++k) load(k);
+  for (int64_t k = 0; k < K; ++k) {
+    const int s = static_cast<int>(k % BULK_STAGES);
+    if (!mbar_wait(&full[s], static_cast<uint32_t>((k / BULK_STAGES) & 1), err)) break;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    bulk_s2g(dst_of[s], stage + (size_t)s * chunk, bytes_of[s]);
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    if (k + BULK_STAGES < K) {
+      // the store just issued must have read its buffer before the refill
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      load(k + BULK_STAGES);
+    }
+  }
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // ring [4][8192] (slot = position & 3) <-> history [3][8192] oldest first, for
@@ -112,14 +157,22 @@ cudaError_t launch_kv_gather(const uint16_t* k_pool, const uint16_t* v_pool,
 }
 
 cudaError_t launch_copy_jobs(const CopyJob* jobs_dev, int32_t n_jobs, const int64_t* chunk_start_dev,
-                             int64_t n_chunks, int32_t chunk, cudaStream_t s) {
+                             int64_t n_chunks, int32_t chunk, int* err, cudaStream_t s) {
   if (n_jobs <= 0 || n_chunks <= 0) return cudaSuccess;
   int dev = 0, nsm = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t grid = std::min<int64_t>(n_chunks, (int64_t)nsm * 8);
-  copy_jobs_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(jobs_dev, n_jobs, chunk_start_dev,
-                                                              n_chunks, chunk);
+  const size_t smem = (size_t)BULK_STAGES * chunk;
+  static int configured_device = -1;
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(copy_jobs_bulk_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured_device = dev;
+  }
+  const int64_t grid = std::min<int64_t>(n_chunks, (int64_t)nsm * QC_BULK_CTAS);
+  copy_jobs_bulk_kernel<<<static_cast<unsigned>(grid), 32, smem, s>>>(
+      jobs_dev, n_jobs, chunk_start_dev, n_chunks, chunk, err);
   return cudaGetLastError();
 }
 

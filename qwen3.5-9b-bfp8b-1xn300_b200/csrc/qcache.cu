@@ -33,7 +33,10 @@ constexpr int PAGE = QC_PAGE;
 constexpr int64_t PAGE_ELEMS = (int64_t)QC_N_HEAD_KV * PAGE * HD;       // per layer, K or V
 constexpr int64_t RING_ELEMS = 4LL * QC_CONV_CH;                        // [4][8192]
 constexpr int64_t HIST_ELEMS = 3LL * QC_CONV_CH;                        // [3][8192]
-constexpr int COPY_CHUNK = 64 * 1024;
+#ifndef QC_COPY_CHUNK_KB
+#define QC_COPY_CHUNK_KB 24
+#endif
+constexpr int COPY_CHUNK = QC_COPY_CHUNK_KB * 1024;  // bulk-copy ring buffer size
 constexpr int STAGING_SLOTS = 4;
 
 struct Seq {
@@ -222,7 +225,7 @@ int run_jobs(qc_ctx* c, const std::vector<CopyJob>& jobs, cudaStream_t s, int64_
   int rc = stage_release(c, si, s);
   if (rc) return rc;
   QC_CUDA(c, qc::launch_copy_jobs(c->jobs, (int32_t)jobs.size(), c->chunk_start, starts.back(),
-                                  COPY_CHUNK, s));
+                                  COPY_CHUNK, c->dev_err, s));
   if (bytes_out) *bytes_out += 2 * total;
   return QC_OK;
 }

@@ -110,6 +110,14 @@ def lib() -> C.CDLL:
 
 
 def _i32arr(xs):
+    """int32 C array from a numpy array (no copy when already int32) or a list."""
+    try:
+        import numpy as np
+        if isinstance(xs, np.ndarray):
+            a = np.ascontiguousarray(xs, dtype=np.int32)
+            return a.ctypes.data_as(PI32)
+    except ImportError:
+        pass
     xs = [int(x) for x in xs]
     return (C.c_int32 * max(1, len(xs)))(*xs)
 
