@@ -414,19 +414,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                           : (row >= t.tile_len) ? smem_u32(sm.zero) : smem_u32(sm.k[s]);
       const uint32_t vb = (row == new_row) ? smem_u32(sm.vnew)
                           : (row >= t.tile_len) ? smem_u32(sm.zero) : smem_u32(sm.v[s]);
-      // ---- S^T = K . Qx^T  (two accumulator chains)
-      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+      // ---- S^T = K . Qx^T  (four accumulator chains)
+      float sa[4][4] = {};
 #pragma unroll
       for (int jj = 0; jj < 8; ++jj) {
         const int d = 32 * jj + 8 * mi;
         const uint32_t addr = kb + (plain ? uint32_t(d * 2) : swz(row, d));
         uint32_t m0, m1, m2, m3;
         ldsm_x4(addr, m0, m1, m2, m3);
-        mma_k16(sa, m0, m1, qb[2 * jj][0], qb[2 * jj][1]);
-        mma_k16(sb, m2, m3, qb[2 * jj + 1][0], qb[2 * jj + 1][1]);
+        mma_k16(sa[(2 * jj) & 3], m0, m1, qb[2 * jj][0], qb[2 * jj][1]);
+        mma_k16(sa[(2 * jj + 1) & 3], m2, m3, qb[2 * jj + 1][0], qb[2 * jj + 1][1]);
       }
       // lane (g, t4): position r0 + g, columns 2t4, 2t4 + 1 -> heads hA, hA + 1
-      float s0 = sa[0] + sb[0], s1 = sa[1] + sb[1];
+      float s0 = (sa[0][0] + sa[1][0]) + (sa[2][0] + sa[3][0]);
+      float s1 = (sa[0][1] + sa[1][1]) + (sa[2][1] + sa[3][1]);
       s0 += __shfl_xor_sync(FULL_MASK, s0, 2);  // hi + lo columns
       s1 += __shfl_xor_sync(FULL_MASK, s1, 2);
       const bool valid = (r0 + g) < t.tile_len;
