@@ -1,8 +1,8 @@
 // gdn_decode.cu — one Gated-DeltaNet decode step, fused in a single
 // memory-bound pass (src/engine.cpp:3204-3327).
 //
-// Work split, small batches (at most 8 sequences): a cluster of R = 8 CTAs per
-// (sequence, v-head), which would otherwise leave most of the 148 SMs idle.
+// Work split, small batches (at most 8 sequences): a cluster of R = 2 or 4 CTAs
+// per (sequence, v-head), which would otherwise leave most of the 148 SMs idle.
 // Large batches use the persistent producer/consumer kernel further down.  CTA r owns state rows
 // [r*128/R, (r+1)*128/R) of the head (rows are independent in the delta rule,
 // src/engine.cpp:3284-3305).  The CTA
@@ -478,7 +478,11 @@ cudaError_t launch_gdn_decode(const GdnArgs& a, cudaStream_t s) {
   // Small batches split each head over a cluster of 8 CTAs to fill the 148
   // SMs; large batches give each (sequence, head) one CTA streaming the whole
   // 64 KiB state slice.
-  if (a.n <= 8) return launch_r<8, 128>(a, s);
+  // Measured on B200 (us/token/layer, batch 1 / 4 / 8): clusters of 4 CTAs
+  // x 256 threads 6.5 / 2.2 / 1.8; clusters of 2 x 256 6.8 / 2.07 / 1.39;
+  // persistent 9.6 / 2.5 / 1.37 and best from 16 up.
+  if (a.n <= 2) return launch_r<4, 256>(a, s);
+  if (a.n <= 8) return launch_r<2, 256>(a, s);
   return launch_persistent(a, s);
 }
 
