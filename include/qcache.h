@@ -48,6 +48,7 @@ extern "C" {
 #define QC_GDN_OUT       4096
 #define QC_GDN_STATE     (QC_GDN_V_HEADS * QC_GDN_HEAD * QC_GDN_HEAD) /* floats per layer per sequence */
 #define QC_PAGE          64                                    /* tokens per KV page */
+#define QC_PREFILL_CHUNK 32                                    /* tokens per prefill call */
 
 /* ---- status codes ---- */
 #define QC_OK            0
@@ -158,6 +159,26 @@ int qc_decode_end(qc_ctx* ctx);
  * them replays correctly after every later qc_decode_begin for the same
  * sequence list. */
 int qc_decode_abort(qc_ctx* ctx);
+
+/* ------------------------------------------------------------------ prefill */
+
+/* Chunked prefill of n <= QC_PREFILL_CHUNK tokens of ONE sequence, positions
+ * len(seq) .. len(seq) + n - 1 — the function the reference computes token by
+ * token in forward_prefill (src/engine.cpp:2602-2722, 2843-2929).  Same
+ * protocol as a decode step: qc_prefill_begin, then every layer, then
+ * qc_prefill_end (commits len += n and records tokens, which may be NULL).
+ *   qc_attn_prefill: proj_dev [n][10240] -> out_dev [n][4096]; appends the n
+ *     K/V rows (same bytes as n decode appends) and attends causally.
+ *   qc_gdn_prefill:  proj_dev [n][12352] -> out_dev [n][4096]; the state is
+ *     read and written once for the chunk.
+ * A prefill and a decode step cannot be open at the same time. */
+int qc_prefill_begin(qc_ctx* ctx, int32_t seq, int32_t n, const int32_t* tokens,
+                     qc_stream stream);
+int qc_attn_prefill(qc_ctx* ctx, int attn_layer, const uint16_t* proj_dev, uint16_t* out_dev,
+                    qc_stream stream);
+int qc_gdn_prefill(qc_ctx* ctx, int gdn_layer, const uint16_t* proj_dev, uint16_t* out_dev,
+                   qc_stream stream);
+int qc_prefill_end(qc_ctx* ctx);
 
 /* ----------------------------------------------------------- prefix cache */
 

@@ -80,6 +80,43 @@ cudaError_t launch_attn_merge_records(const float* records, int32_t n_parts, con
 // Message returned by qc_last_error(NULL) on this thread (qcache.cu).
 void set_thread_error(const char* msg);
 
+// Chunked prefill of T <= QC_PREFILL_CHUNK tokens of one sequence (prefill.cu).
+struct GdnPrefillArgs {
+  const uint16_t* proj;      // [T][12352] bf16
+  uint16_t* out;             // [T][4096] bf16
+  float* state;              // this sequence's state of this layer [32][128][128]
+  uint16_t* ring;            // this sequence's conv ring of this layer [4][8192]
+  const float* conv_w;
+  const float* ssm_a;
+  const float* dt_bias;
+  const float* ssm_norm;
+  int32_t pos0;              // position of the chunk's first token
+  int32_t T;
+};
+cudaError_t launch_gdn_prefill(const GdnPrefillArgs& a, cudaStream_t s);
+
+struct AttnPrefillArgs {
+  const uint16_t* proj;      // [T][10240] bf16
+  uint16_t* out;             // [T][4096] bf16
+  uint16_t* k_pool;          // this layer
+  uint16_t* v_pool;
+  const int32_t* page_row;   // this sequence's page-table row
+  int32_t max_pages;
+  const float* q_norm;
+  const float* k_norm;
+  const float* rope_cos;
+  const float* rope_sin;
+  uint16_t* q_buf;           // scratch [4 kv-heads][128 rows][256] bf16, row = head * 32 + t
+  float* rec;                // scratch [4][n_split][128 rows][258] f32
+  int32_t pos0;
+  int32_t T;
+  int32_t n_split;           // CTAs per kv-head
+  int* err;
+};
+cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, const CUtensorMap& tmk,
+                                const CUtensorMap& tmv, cudaStream_t s);
+int attn_prefill_smem_bytes();
+
 // Copies (kv_copy.cu).
 // Scatter / gather of positions [pos0, pos0 + n) of one sequence between a
 // contiguous [n][4][256] array and the paged pool of one layer.

@@ -92,6 +92,9 @@ struct qc_ctx {
   int64_t* chunk_start = nullptr;
   int32_t job_cap = 0;
   int* dev_err = nullptr;
+  uint16_t* pf_q = nullptr;     // prefill: q tile [4][128][256] bf16
+  float* pf_rec = nullptr;      // prefill: records [4][pf_split][128][258] f32
+  int32_t pf_split = 0;
   std::vector<CUtensorMap> tm_k, tm_v;  // per attention layer, for the TMA tile loads
 
   // pinned staging ring for host -> device uploads
@@ -115,6 +118,10 @@ struct qc_ctx {
   bool b_has_tok = false;
   int32_t b_total = 0, b_per = 0, b_grid = 0;
   int64_t last_restore_bytes = 0;
+  // open prefill chunk
+  bool in_prefill = false;
+  int32_t p_seq = -1, p_pos0 = 0, p_n = 0;
+  std::vector<int32_t> p_tok;
 };
 
 namespace {
@@ -332,6 +339,7 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
   const int na = cfg->n_attn_layers, ng = cfg->n_gdn_layers;
   const int64_t pool = (int64_t)std::max(na, 1) * cfg->max_pages * PAGE_ELEMS;
   c->part_slots = 4 * cfg->max_batch + c->nsm + 8;
+  c->pf_split = (c->nsm + 3) / 4;
   c->job_cap = cfg->max_batch * (1 + 3 * std::max(ng, 1) + 2 * na) + 64;
   struct A { void** p; size_t bytes; const char* what; };
   const A allocs[] = {
@@ -358,6 +366,9 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
       {(void**)&c->jobs, (size_t)c->job_cap * sizeof(CopyJob), "jobs"},
       {(void**)&c->chunk_start, (size_t)(c->job_cap + 1) * 8, "chunk_start"},
       {(void**)&c->dev_err, 16, "dev_err"},
+      {(void**)&c->pf_q, (size_t)4 * 4 * QC_PREFILL_CHUNK * HD * 2, "prefill q"},
+      {(void**)&c->pf_rec, (size_t)4 * c->pf_split * 4 * QC_PREFILL_CHUNK * (HD + 2) * 4,
+       "prefill records"},
   };
   for (const A& a : allocs) {
     e = cudaMalloc(a.p, a.bytes);
@@ -429,7 +440,7 @@ void qc_destroy(qc_ctx* c) {
     cudaDeviceSynchronize();
     void* ptrs[] = {c->k_pool, c->v_pool, c->state, c->ring, c->snap_state, c->snap_hist,
                     c->q_norm, c->k_norm, c->ssm_a, c->dt_bias, c->ssm_norm, c->conv_w,
-                    c->rope_cos, c->rope_sin, c->page_table, c->desc, c->desc_part,
+                    c->rope_cos, c->rope_sin, c->page_table, c->desc, c->desc_part, c->pf_q, c->pf_rec,
                     c->part_m, c->part_l,
                     c->part_o, c->jobs, c->chunk_start, c->dev_err};
     for (void* p : ptrs)
@@ -494,7 +505,7 @@ int qc_seq_alloc(qc_ctx* c, int32_t* seq) {
 int qc_seq_reset(qc_ctx* c, int32_t s, qc_stream stream) {
   if (!c) return QC_ERR_ARG;
   if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
-  if (c->in_step) return fail(c, QC_ERR_ARG, "reset inside a decode step");
+  if (c->in_step || c->in_prefill) return fail(c, QC_ERR_ARG, "reset inside an open step");
   free_seq_pages(c, s);
   c->seqs[s].len = 0;
   c->seqs[s].tokens.clear();
@@ -512,7 +523,7 @@ int qc_seq_reset(qc_ctx* c, int32_t s, qc_stream stream) {
 int qc_seq_free(qc_ctx* c, int32_t s) {
   if (!c) return QC_ERR_ARG;
   if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
-  if (c->in_step) return fail(c, QC_ERR_ARG, "free inside a decode step");
+  if (c->in_step || c->in_prefill) return fail(c, QC_ERR_ARG, "free inside an open step");
   free_seq_pages(c, s);
   c->seqs[s] = Seq();
   return QC_OK;
@@ -536,7 +547,7 @@ int qc_seq_pages(const qc_ctx* c, int32_t s, int32_t* pages, int32_t cap, int32_
 int qc_seq_reserve(qc_ctx* c, int32_t s, int32_t new_len) {
   if (!c) return QC_ERR_ARG;
   if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
-  if (c->in_step) return fail(c, QC_ERR_ARG, "reserve inside a decode step");
+  if (c->in_step || c->in_prefill) return fail(c, QC_ERR_ARG, "reserve inside an open step");
   Seq& q = c->seqs[s];
   if (new_len < q.len || new_len > c->cfg.max_ctx)
     return fail(c, QC_ERR_ARG, "reserve %d: length %d, max_ctx %d", new_len, q.len, c->cfg.max_ctx);
@@ -634,6 +645,7 @@ int qc_decode_begin(qc_ctx* c, const int32_t* seq_ids, int32_t n, const int32_t*
                     qc_stream stream) {
   if (!c || !seq_ids) return QC_ERR_ARG;
   if (c->in_step) return fail(c, QC_ERR_ARG, "decode step already open");
+  if (c->in_prefill) return fail(c, QC_ERR_ARG, "prefill chunk open");
   if (n <= 0 || n > c->cfg.max_batch)
     return fail(c, QC_ERR_ARG, "batch of %d (max_batch %d)", n, c->cfg.max_batch);
   cudaStream_t st = (cudaStream_t)stream;
@@ -792,6 +804,114 @@ int qc_decode_abort(qc_ctx* c) {
   return QC_OK;
 }
 
+// ------------------------------------------------------------------ prefill
+
+int qc_prefill_begin(qc_ctx* c, int32_t s, int32_t n, const int32_t* tokens, qc_stream stream) {
+  if (!c) return QC_ERR_ARG;
+  if (c->in_step || c->in_prefill) return fail(c, QC_ERR_ARG, "a step is already open");
+  if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
+  if (n < 1 || n > QC_PREFILL_CHUNK)
+    return fail(c, QC_ERR_ARG, "prefill of %d tokens (1..%d)", n, QC_PREFILL_CHUNK);
+  Seq& q = c->seqs[s];
+  if (q.len + n > c->cfg.max_ctx)
+    return fail(c, QC_ERR_ARG, "sequence %d: %d + %d tokens exceed max_ctx %d", s, q.len, n,
+                c->cfg.max_ctx);
+  std::vector<CopyJob> cow;
+  const int32_t first = q.len / PAGE, last = (q.len + n - 1) / PAGE;
+  if (first < (int32_t)q.pages.size() && c->page_ref[q.pages[first]] > 1) {  // shared tail
+    const int32_t p = page_alloc(c);
+    if (p < 0) return fail(c, QC_ERR_OOM, "KV page pool exhausted (%d pages)", c->cfg.max_pages);
+    if (!c->host_only) page_copy_jobs(c, q.pages[first], p, cow);
+    page_decref(c, q.pages[first]);
+    q.pages[first] = p;
+  }
+  const size_t before = q.pages.size();
+  while ((int32_t)q.pages.size() <= last) {
+    const int32_t p = page_alloc(c);
+    if (p < 0) {
+      while (q.pages.size() > before) {
+        page_decref(c, q.pages.back());
+        q.pages.pop_back();
+      }
+      return fail(c, QC_ERR_OOM, "KV page pool exhausted (%d pages)", c->cfg.max_pages);
+    }
+    q.pages.push_back(p);
+  }
+  set_row(c, s);
+  if (!c->host_only) {
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = run_jobs(c, cow, st, nullptr);
+    if (rc) return rc;
+    if ((rc = sync_rows(c, st))) return rc;
+  }
+  c->in_prefill = true;
+  c->p_seq = s;
+  c->p_pos0 = q.len;
+  c->p_n = n;
+  c->p_tok.clear();
+  if (tokens) c->p_tok.assign(tokens, tokens + n);
+  return QC_OK;
+}
+
+int qc_attn_prefill(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc_stream stream) {
+  if (!c || !proj || !out) return QC_ERR_ARG;
+  if (!c->in_prefill) return fail(c, QC_ERR_ARG, "no open prefill chunk");
+  if (layer < 0 || layer >= c->cfg.n_attn_layers) return fail(c, QC_ERR_ARG, "attn layer %d", layer);
+  QC_NEED_DEVICE(c);
+  const int64_t base = (int64_t)layer * c->cfg.max_pages * PAGE_ELEMS;
+  qc::AttnPrefillArgs a{};
+  a.proj = proj;
+  a.out = out;
+  a.k_pool = c->k_pool + base;
+  a.v_pool = c->v_pool + base;
+  a.page_row = c->page_table + (int64_t)c->p_seq * c->pt_stride;
+  a.max_pages = c->cfg.max_pages;
+  a.q_norm = c->q_norm + layer * HD;
+  a.k_norm = c->k_norm + layer * HD;
+  a.rope_cos = c->rope_cos;
+  a.rope_sin = c->rope_sin;
+  a.q_buf = c->pf_q;
+  a.rec = c->pf_rec;
+  a.pos0 = c->p_pos0;
+  a.T = c->p_n;
+  const int32_t n_pages = (c->p_pos0 + c->p_n + PAGE - 1) / PAGE;
+  a.n_split = std::min(c->pf_split, n_pages);
+  a.err = c->dev_err;
+  QC_CUDA(c, qc::launch_attn_prefill(a, c->tm_k[layer], c->tm_v[layer], (cudaStream_t)stream));
+  return QC_OK;
+}
+
+int qc_gdn_prefill(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc_stream stream) {
+  if (!c || !proj || !out) return QC_ERR_ARG;
+  if (!c->in_prefill) return fail(c, QC_ERR_ARG, "no open prefill chunk");
+  if (layer < 0 || layer >= c->cfg.n_gdn_layers) return fail(c, QC_ERR_ARG, "gdn layer %d", layer);
+  QC_NEED_DEVICE(c);
+  qc::GdnPrefillArgs g{};
+  g.proj = proj;
+  g.out = out;
+  g.state = slot_state(c, c->p_seq, layer);
+  g.ring = slot_ring(c, c->p_seq, layer);
+  g.conv_w = c->conv_w + (int64_t)layer * 4 * QC_CONV_CH;
+  g.ssm_a = c->ssm_a + layer * 32;
+  g.dt_bias = c->dt_bias + layer * 32;
+  g.ssm_norm = c->ssm_norm + layer * 128;
+  g.pos0 = c->p_pos0;
+  g.T = c->p_n;
+  QC_CUDA(c, qc::launch_gdn_prefill(g, (cudaStream_t)stream));
+  return QC_OK;
+}
+
+int qc_prefill_end(qc_ctx* c) {
+  if (!c) return QC_ERR_ARG;
+  if (!c->in_prefill) return fail(c, QC_ERR_ARG, "no open prefill chunk");
+  Seq& q = c->seqs[c->p_seq];
+  if (!c->p_tok.empty() && q.tokens.size() == (size_t)q.len)
+    q.tokens.insert(q.tokens.end(), c->p_tok.begin(), c->p_tok.end());
+  q.len += c->p_n;
+  c->in_prefill = false;
+  return QC_OK;
+}
+
 // ------------------------------------------------------------- prefix cache
 
 int qc_seq_match_prefix(qc_ctx* c, int32_t s, const int32_t* tokens, int32_t n,
@@ -833,7 +953,7 @@ int qc_prefix_insert(qc_ctx* c, int32_t s, const int32_t* tokens, int32_t n, int
                      qc_stream stream) {
   if (!c || !tokens || !entry || n <= 0) return QC_ERR_ARG;
   if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
-  if (c->in_step) return fail(c, QC_ERR_ARG, "insert inside a decode step");
+  if (c->in_step || c->in_prefill) return fail(c, QC_ERR_ARG, "insert inside an open step");
   Seq& q = c->seqs[s];
   if (q.len != n) return fail(c, QC_ERR_ARG, "sequence length %d != %d tokens", q.len, n);
   if (q.tokens.size() == (size_t)n && !std::equal(tokens, tokens + n, q.tokens.begin()))
@@ -920,7 +1040,7 @@ int qc_prefix_lookup(qc_ctx* c, const int32_t* tokens, int32_t n, int32_t* match
 int qc_prefix_restore(qc_ctx* c, const int32_t* entries, const int32_t* seqs, int32_t n,
                       qc_stream stream) {
   if (!c || !entries || !seqs || n < 0) return QC_ERR_ARG;
-  if (c->in_step) return fail(c, QC_ERR_ARG, "restore inside a decode step");
+  if (c->in_step || c->in_prefill) return fail(c, QC_ERR_ARG, "restore inside an open step");
   for (int32_t i = 0; i < n; ++i) {
     if (entries[i] < 0 || entries[i] >= (int32_t)c->entries.size() || !c->entries[entries[i]].live)
       return fail(c, QC_ERR_ARG, "entry %d is not live", entries[i]);

@@ -89,6 +89,10 @@ def lib() -> C.CDLL:
         "qc_gdn_decode": (C.c_int, [P, C.c_int, P, P, P]),
         "qc_decode_end": (C.c_int, [P]),
         "qc_decode_abort": (C.c_int, [P]),
+        "qc_prefill_begin": (C.c_int, [P, I32, I32, PI32, P]),
+        "qc_attn_prefill": (C.c_int, [P, C.c_int, P, P, P]),
+        "qc_gdn_prefill": (C.c_int, [P, C.c_int, P, P, P]),
+        "qc_prefill_end": (C.c_int, [P]),
         "qc_seq_match_prefix": (C.c_int, [P, I32, PI32, I32, PI32, P]),
         "qc_prefix_insert": (C.c_int, [P, I32, PI32, I32, PI32, P]),
         "qc_prefix_lookup": (C.c_int, [P, PI32, I32, PI32, PI32]),
@@ -224,6 +228,20 @@ class QCache:
 
     def decode_abort(self):
         self._ck(self.L.qc_decode_abort(self.h))
+
+    # ---- prefill
+    def prefill_begin(self, s, n, tokens=None, stream=0):
+        tok = _i32arr(tokens) if tokens is not None else None
+        self._ck(self.L.qc_prefill_begin(self.h, s, n, tok, stream))
+
+    def attn_prefill(self, layer, proj_ptr, out_ptr, stream=0):
+        self._ck(self.L.qc_attn_prefill(self.h, layer, proj_ptr, out_ptr, stream))
+
+    def gdn_prefill(self, layer, proj_ptr, out_ptr, stream=0):
+        self._ck(self.L.qc_gdn_prefill(self.h, layer, proj_ptr, out_ptr, stream))
+
+    def prefill_end(self):
+        self._ck(self.L.qc_prefill_end(self.h))
 
     # ---- prefix cache
     def match_prefix(self, s, tokens, stream=0) -> int:

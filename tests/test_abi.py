@@ -165,3 +165,20 @@ def test_restore_requires_empty_sequence(qcache):
         q.prefix_restore([e], [s])                       # s is not empty
     with pytest.raises(qcache.QCacheError):
         q.prefix_restore([e + 5], [q.seq_alloc()])       # no such entry
+
+
+def test_prefill_bookkeeping(qcache):
+    q = host_ctx(qcache)
+    s = q.seq_alloc()
+    q.prefill_begin(s, 32, tokens=list(range(32)))
+    with pytest.raises(qcache.QCacheError):
+        q.decode_begin([s])                          # one open step at a time
+    q.prefill_end()
+    q.prefill_begin(s, 32, tokens=list(range(32, 64)))
+    q.prefill_end()
+    q.prefill_begin(s, 1, tokens=[64])
+    q.prefill_end()
+    assert q.seq_len(s) == 65 and len(q.seq_pages(s)) == 2
+    assert q.match_prefix(s, list(range(65)) + [7]) == 65
+    with pytest.raises(qcache.QCacheError):
+        q.prefill_begin(s, 33)                       # chunk limit
