@@ -596,6 +596,79 @@ def run_prefix(args):
                 decode_us_token_layer=decode_ms * 1e3 / (n * N_LAYERS))
 
 
+def run_prefill(args, prompt=2048):
+    """Prefill of one `prompt`-token sequence through the 32-layer stack in
+    chunks of QC_PREFILL_CHUNK tokens (the reference prefills token by token,
+    src/engine.cpp:2602, 2843), and the same prompt as one decode step per
+    token for comparison."""
+    import torch
+    qc = load_pkg("qcache")
+    synth = load_pkg("synth")
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    stream = torch.cuda.current_stream().cuda_stream
+    kinds = [("a" if is_attn(l) else "g") for l in range(N_LAYERS)]
+    chunk = 32
+    q = qc.QCache(n_attn_layers=N_ATTN, n_gdn_layers=N_GDN, max_seqs=2,
+                  max_pages=2 * (prompt // 64 + 2), max_ctx=prompt + 64, max_batch=1,
+                  max_snapshots=1, device=torch.cuda.current_device())
+    for l in range(N_ATTN):
+        a = synth.attn_inputs(l, 1, 0)
+        q.set_attn_params(l, a["q_norm"], a["k_norm"])
+    for l in range(N_GDN):
+        p = synth.gdn_params(100 + l)
+        q.set_gdn_params(l, p["ssm_a"], p["dt_bias"], p["ssm_norm"], p["conv_w"])
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    bf16 = torch.bfloat16
+    proj = [torch.randn(chunk, 10240 if kd == "a" else 12352, generator=g, device="cuda").to(bf16)
+            for kd in kinds]
+    out = [torch.empty(chunk, 4096, device="cuda", dtype=bf16) for _ in kinds]
+
+    def prefill(s, n_tok):
+        for c0 in range(0, n_tok, chunk):
+            n = min(chunk, n_tok - c0)
+            q.prefill_begin(s, n, stream=stream)
+            ai = gi = 0
+            for l, kd in enumerate(kinds):
+                if kd == "a":
+                    q.attn_prefill(ai, proj[l].data_ptr(), out[l].data_ptr(), stream)
+                    ai += 1
+                else:
+                    q.gdn_prefill(gi, proj[l].data_ptr(), out[l].data_ptr(), stream)
+                    gi += 1
+            q.prefill_end()
+
+    def decode(s, n_tok):
+        for _ in range(n_tok):
+            q.decode_begin([s], stream=stream)
+            ai = gi = 0
+            for l, kd in enumerate(kinds):
+                if kd == "a":
+                    q.attn_decode(ai, proj[l].data_ptr(), out[l].data_ptr(), stream)
+                    ai += 1
+                else:
+                    q.gdn_decode(gi, proj[l].data_ptr(), out[l].data_ptr(), stream)
+                    gi += 1
+            q.decode_end()
+
+    s = q.seq_alloc()
+    prefill(s, 256)                    # warm-up
+    q.seq_reset(s, stream)
+    torch.cuda.synchronize()
+    res = {}
+    for name, fn in (("prefill", prefill), ("decode", decode)):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn(s, prompt)
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1)
+        q.seq_reset(s, stream)
+        torch.cuda.synchronize()
+    q.check_device()
+    return res, prompt
+
+
 # ------------------------------------------------------------ CPU baseline
 
 
@@ -670,7 +743,8 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(WORKLOADS) + ["prefix"], default="stack",
+    ap.add_argument("--config", choices=sorted(WORKLOADS) + ["prefix", "prefill"],
+                    default="stack",
                     help="stack = the headline workload; the others are the baseline's "
                          "per-component configurations")
     ap.add_argument("--seqs", type=int, default=None,
@@ -700,7 +774,19 @@ def main():
                            "peak_kind": peak_kind, "unit": "GB/s",
                            "frac": round(r["restore_gbs"] / peak, 4), "traffic": None}})
         return
-    if args.config == "prefix":
+    if args.config == "prefill" and args.impl == "ours":
+        r, prompt = run_prefill(args)
+        emit({"metric": "prefill cache-path us/token/layer", "value":
+              round(r["prefill"] * 1e3 / (prompt * N_LAYERS), 4), "unit": "us", "n_gpus": 1,
+              "higher_is_better": False, "dtype": "f32", "data": "synthetic (seeded)",
+              "config": {"workload": f"prefill of one {prompt}-token prompt through the 32-layer "
+                                     "stack in chunks of 32 tokens", "name": "prefill"},
+              "prefill_ms": round(r["prefill"], 3), "prefill_tokens_per_s":
+              round(prompt / (r["prefill"] * 1e-3), 1),
+              "token_by_token_decode_ms": round(r["decode"], 3),
+              "speedup_vs_token_by_token": round(r["decode"] / r["prefill"], 2)})
+        return
+    if args.config in ("prefix", "prefill"):
         args.config = "stack"
     kinds, n_total, ctx, desc = WORKLOADS[args.config]
     if args.seqs:

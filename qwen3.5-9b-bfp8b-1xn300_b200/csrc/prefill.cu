@@ -3,13 +3,14 @@
 // (src/engine.cpp:2602-2722 DeltaNet, :2843-2929 attention); these kernels
 // compute the same function for a whole chunk per launch.
 //
-// DeltaNet (gdn_prefill_kernel): one CTA per v-head.  Phase A computes, for
-// every token of the chunk in parallel, the causal conv + SiLU of the head's
-// q, k and v channels (history from the conv ring, then the chunk's own
-// inputs), the L2 norms, decay and beta.  Phase B keeps the head's 128 x 128
-// fp32 state in registers (8 warps x 16 rows, one float4 per lane and row)
-// and runs the delta rule token after token — the state is read from and
-// written to HBM once per chunk instead of once per token.  Phase C applies
+// DeltaNet (gdn_prefill_kernel): a cluster of 8 CTAs per v-head, CTA r owning
+// 16 of the head's 128 state rows.  Phase A computes, for every token of the
+// chunk in parallel, the causal conv + SiLU of the head's q and k channels and
+// of the CTA's v channels (history from the conv ring, then the chunk's own
+// inputs), the L2 norms, decay and beta.  Phase B keeps the CTA's rows of the
+// fp32 state in registers (2 rows per warp, one float4 per lane and row) and
+// runs the delta rule token after token — the state is read from and written
+// to HBM once per chunk instead of once per token.  Phase C applies
 // the gated RMSNorm per token.  The conv ring is advanced by a separate
 // launch after all heads have read it (gdn_prefill_ring_kernel).
 //
@@ -24,8 +25,12 @@
 // (m, l, o) record per row.  prefill_combine_kernel merges the page ranges and
 // applies the output gate.  Q enters the MMAs rounded to bf16 (decode keeps
 // a bf16 residual as well); the error this adds is ~1e-3 relative.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace qc {
 namespace {
@@ -45,29 +50,42 @@ constexpr int BOX_ROWS = 16;
 constexpr int BOX_BYTES = BOX_ROWS * 128;
 constexpr float SCALE_LOG2 = 0.0625f * 1.4426950408889634f;
 
+constexpr int GR = 8;            // CTAs per v-head (a cluster)
+constexpr int GRB = HK / GR;     // state rows per CTA
+constexpr int GRPW = GRB / 8;    // rows per warp
+
 struct GdnPrefillSmem {
   float q[TMAX][HK];
   float k[TMAX][HK];
-  float v[TMAX][HK];
-  float o[TMAX][HK];
+  float v[TMAX][GRB];
+  float o[TMAX][GRB];
   float decay[TMAX];
   float beta[TMAX];
-  float rms[TMAX];
+  float ssq[GR][TMAX];          // per-token partial sums of squares, slot per CTA
 };
 
+// Cluster of GR CTAs per v-head; CTA r owns state rows [r*GRB, (r+1)*GRB).
 __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArgs a) {
   extern __shared__ __align__(16) unsigned char raw[];
   GdnPrefillSmem& sm = *reinterpret_cast<GdnPrefillSmem*>(raw);
+  cg::cluster_group cluster = cg::this_cluster();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int vh = blockIdx.x, kh = vh & 15;  // kh = vh % 16 (src/engine.cpp:3254)
+  const int vh = blockIdx.x / GR, r = static_cast<int>(cluster.block_rank());
+  const int kh = vh & 15;  // kh = vh % 16 (src/engine.cpp:3254)
   const int T = a.T, pos0 = a.pos0;
   const float* w = a.conv_w;
+  // first half of a split cluster barrier: peers may write our shared memory
+  // after their matching wait
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
-  // ---- phase A: conv + SiLU of q, k, v for every token (src/engine.cpp:3204-3234)
-  for (int idx = tid; idx < T * 3 * HK; idx += 256) {
-    const int t = idx / (3 * HK), ch = idx % (3 * HK);
+  // ---- phase A: conv + SiLU of q, k (all 128 channels) and of this CTA's v
+  // channels, every token of the chunk (src/engine.cpp:3204-3234)
+  constexpr int NCH = 2 * HK + GRB;
+  for (int idx = tid; idx < T * NCH; idx += 256) {
+    const int t = idx / NCH, ch = idx % NCH;
     const int c = (ch < HK) ? kh * HK + ch
-                : (ch < 2 * HK) ? 2048 + kh * HK + (ch - HK) : 4096 + vh * HK + (ch - 2 * HK);
+                : (ch < 2 * HK) ? 2048 + kh * HK + (ch - HK)
+                                : 4096 + vh * HK + r * GRB + (ch - 2 * HK);
     float xs[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -92,8 +110,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArg
     sm.beta[tid] = sigmoid_exact(bf2f(x[12320 + vh]));
   }
   __syncthreads();
-  // L2 normalisation of q and k per token (src/engine.cpp:3261-3275): warp
-  // per token, lane holds 4 of the 128 values
+  // L2 normalisation of q and k per token (src/engine.cpp:3261-3275)
   for (int t = warp; t < T; t += 8) {
     float4 q4 = reinterpret_cast<float4*>(sm.q[t])[lane];
     float4 k4 = reinterpret_cast<float4*>(sm.k[t])[lane];
@@ -107,70 +124,79 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArg
   }
   __syncthreads();
 
-  // ---- phase B: delta rule token by token, state rows in registers
-  float* st = a.state + (int64_t)vh * HK * HK;
-  float4 S[16];
+  // ---- phase B: delta rule token by token, this warp's rows in registers
+  const int row0 = warp * GRPW;  // local row
+  float* st = a.state + (int64_t)vh * HK * HK + (int64_t)r * GRB * HK;
+  float4 S[GRPW];
 #pragma unroll
-  for (int r = 0; r < 16; ++r) S[r] = reinterpret_cast<const float4*>(st)[(warp * 16 + r) * 32 + lane];
+  for (int i = 0; i < GRPW; ++i) S[i] = reinterpret_cast<const float4*>(st)[(row0 + i) * 32 + lane];
   for (int t = 0; t < T; ++t) {
     const float4 k4 = reinterpret_cast<const float4*>(sm.k[t])[lane];
     const float4 q4 = reinterpret_cast<const float4*>(sm.q[t])[lane];
     const float dec = sm.decay[t], bt = sm.beta[t];
-    float sk[16];
+    float sk[GRPW];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      S[r].x *= dec; S[r].y *= dec; S[r].z *= dec; S[r].w *= dec;
-      float d = S[r].x * k4.x;
-      d = fmaf(S[r].y, k4.y, d);
-      d = fmaf(S[r].z, k4.z, d);
-      d = fmaf(S[r].w, k4.w, d);
-      sk[r] = d;
+    for (int i = 0; i < GRPW; ++i) {
+      S[i].x *= dec; S[i].y *= dec; S[i].z *= dec; S[i].w *= dec;
+      float d = S[i].x * k4.x;
+      d = fmaf(S[i].y, k4.y, d);
+      d = fmaf(S[i].z, k4.z, d);
+      d = fmaf(S[i].w, k4.w, d);
+      sk[i] = d;
     }
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1)
 #pragma unroll
-      for (int r = 0; r < 16; ++r) sk[r] += __shfl_xor_sync(FULL_MASK, sk[r], m);
-    float o[16];
+      for (int i = 0; i < GRPW; ++i) sk[i] += __shfl_xor_sync(FULL_MASK, sk[i], m);
+    float o[GRPW];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const float dd = bt * (sm.v[t][warp * 16 + r] - sk[r]);
-      S[r].x = fmaf(k4.x, dd, S[r].x);
-      S[r].y = fmaf(k4.y, dd, S[r].y);
-      S[r].z = fmaf(k4.z, dd, S[r].z);
-      S[r].w = fmaf(k4.w, dd, S[r].w);
-      float d = S[r].x * q4.x;
-      d = fmaf(S[r].y, q4.y, d);
-      d = fmaf(S[r].z, q4.z, d);
-      d = fmaf(S[r].w, q4.w, d);
-      o[r] = d;
+    for (int i = 0; i < GRPW; ++i) {
+      const float dd = bt * (sm.v[t][row0 + i] - sk[i]);
+      S[i].x = fmaf(k4.x, dd, S[i].x);
+      S[i].y = fmaf(k4.y, dd, S[i].y);
+      S[i].z = fmaf(k4.z, dd, S[i].z);
+      S[i].w = fmaf(k4.w, dd, S[i].w);
+      float d = S[i].x * q4.x;
+      d = fmaf(S[i].y, q4.y, d);
+      d = fmaf(S[i].z, q4.z, d);
+      d = fmaf(S[i].w, q4.w, d);
+      o[i] = d;
     }
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1)
 #pragma unroll
-      for (int r = 0; r < 16; ++r) o[r] += __shfl_xor_sync(FULL_MASK, o[r], m);
-    if (lane < 16) {
+      for (int i = 0; i < GRPW; ++i) o[i] += __shfl_xor_sync(FULL_MASK, o[i], m);
+    if (lane < GRPW) {
       float ov = o[0];
 #pragma unroll
-      for (int r = 1; r < 16; ++r) ov = (lane == r) ? o[r] : ov;
-      sm.o[t][warp * 16 + lane] = ov * SSM_SCALE;
+      for (int i = 1; i < GRPW; ++i) ov = (lane == i) ? o[i] : ov;
+      sm.o[t][row0 + lane] = ov * SSM_SCALE;
     }
   }
 #pragma unroll
-  for (int r = 0; r < 16; ++r) reinterpret_cast<float4*>(st)[(warp * 16 + r) * 32 + lane] = S[r];
+  for (int i = 0; i < GRPW; ++i) reinterpret_cast<float4*>(st)[(row0 + i) * 32 + lane] = S[i];
   __syncthreads();
 
-  // ---- phase C: gated RMSNorm per token (src/engine.cpp:3307-3322)
+  // ---- phase C: gated RMSNorm per token (src/engine.cpp:3307-3322); the
+  // per-token partial sums of squares of the cluster's CTAs meet in every
+  // CTA's shared memory (plain remote stores), then one cluster barrier
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // peers have started
   for (int t = warp; t < T; t += 8) {
-    const float4 o4 = reinterpret_cast<const float4*>(sm.o[t])[lane];
-    const float ss = warp_sum(o4.x * o4.x + o4.y * o4.y + o4.z * o4.z + o4.w * o4.w);
-    if (lane == 0) sm.rms[t] = 1.0f / sqrtf(ss / 128.0f + EPS);
+    float x = (lane < GRB) ? sm.o[t][lane] : 0.0f;
+    const float ss = warp_sum(x * x);
+    if (lane < GR) *cluster.map_shared_rank(&sm.ssq[r][t], lane) = ss;
   }
-  __syncthreads();
-  for (int idx = tid; idx < T * HK; idx += 256) {
-    const int t = idx / HK, d = idx % HK;
-    const float z = bf2f(a.proj[(int64_t)t * 12352 + 8192 + vh * HK + d]);
-    const float y = (sm.o[t][d] * sm.rms[t]) * a.ssm_norm[d] * silu_exact(z);
-    a.out[(int64_t)t * 4096 + vh * HK + d] = f2bf(y);
+  cluster.sync();
+  for (int idx = tid; idx < T * GRB; idx += 256) {
+    const int t = idx / GRB, d = idx % GRB;
+    float tot = 0.0f;
+#pragma unroll
+    for (int q = 0; q < GR; ++q) tot += sm.ssq[q][t];
+    const float rms = 1.0f / sqrtf(tot / 128.0f + EPS);
+    const int dd = r * GRB + d;
+    const float z = bf2f(a.proj[(int64_t)t * 12352 + 8192 + vh * HK + dd]);
+    const float y = (sm.o[t][d] * rms) * a.ssm_norm[dd] * silu_exact(z);
+    a.out[(int64_t)t * 4096 + vh * HK + dd] = f2bf(y);
   }
 }
 
@@ -476,8 +502,19 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs& a, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     configured_device = dev;
   }
-  gdn_prefill_kernel<<<32, 256, sizeof(GdnPrefillSmem), s>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(32 * GR, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = sizeof(GdnPrefillSmem);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = GR;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gdn_prefill_kernel, a);
   if (e != cudaSuccess) return e;
   gdn_prefill_ring_kernel<<<CONV / 256, 256, 0, s>>>(a);
   return cudaGetLastError();
