@@ -107,7 +107,7 @@ struct AttnPrefillArgs {
   const float* rope_cos;
   const float* rope_sin;
   uint16_t* q_buf;           // scratch [4 kv-heads][128 rows][256] bf16, row = head * 32 + t
-  float* rec;                // scratch [4][n_split][128 rows][258] f32
+  float* rec;                // scratch [4][n_split][128 rows][260] f32 (m, l, pad, o)
   int32_t pos0;
   int32_t T;
   int32_t n_split;           // CTAs per kv-head

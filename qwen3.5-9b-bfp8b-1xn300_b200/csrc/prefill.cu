@@ -44,11 +44,10 @@ constexpr int HD = 256;
 constexpr int PAGE = 64;
 constexpr int ROWS = 4 * TMAX;                // query rows per kv-head: 4 heads x 32 tokens
 constexpr int PSTAGES = 2;
-constexpr int PCONS = ROWS / 16;              // consumer warps, 16 rows each
-constexpr int PTHREADS = (PCONS + 1) * 32;
 constexpr int BOX_ROWS = 16;
 constexpr int BOX_BYTES = BOX_ROWS * 128;
 constexpr float SCALE_LOG2 = 0.0625f * 1.4426950408889634f;
+constexpr int REC = HD + 4;                   // record: m, l, 2 pad, o[256] (16 B aligned)
 
 constexpr int GR = 8;            // CTAs per v-head (a cluster)
 constexpr int GRB = HK / GR;     // state rows per CTA
@@ -254,35 +253,9 @@ __global__ void __launch_bounds__(640) prefill_qk_kernel(const AttnPrefillArgs a
       *reinterpret_cast<const uint4*>(prow + 9216 + kvh * HD + lane * 8);
 }
 
-struct __align__(1024) PrefillSmem {
-  uint16_t k[PSTAGES][PAGE * HD];   // swizzled tiles, as in decode
-  uint16_t v[PSTAGES][PAGE * HD];
-  uint16_t q[ROWS * HD];            // swizzled: [col block 4][row 128][128 B]
-  uint64_t full[PSTAGES];
-  uint64_t empty[PSTAGES];
-};
-
 // byte offset of (row, dim) in a swizzled tile of `rows` rows
 __device__ __forceinline__ uint32_t pswz(int row, int dim, int rows) {
   return (uint32_t)((dim >> 6) * (rows * 128) + row * 128 + ((((dim & 63) >> 3) ^ (row & 7)) << 4));
-}
-__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t (&r)[4]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm4t(uint32_t addr, uint32_t (&r)[4]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return uint32_t(f2bf(lo)) | (uint32_t(f2bf(hi)) << 16);
@@ -296,174 +269,289 @@ __device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* map, int x, 
       : "memory");
 }
 
-__global__ void __launch_bounds__(PTHREADS, 1)
-    attn_prefill_kernel(const AttnPrefillArgs a, const __grid_constant__ CUtensorMap tmk,
-                        const __grid_constant__ CUtensorMap tmv) {
+// ---------------------------------------------------- tcgen05 flash pass
+
+// UMMA shared-memory descriptor of a 128-byte-swizzled tile (layout type 2,
+// descriptor version 1), start / leading / stride byte offsets in 16 B units.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// D (TMEM, f32) (+)= A (smem) . B (smem), kind::f16 with bf16 operands
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+// arrive on `bar` when every tcgen05.mma issued so far by this thread is done
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// 32 consecutive f32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+constexpr int TC_SOFTMAX = 4;                  // warps: one query row per thread
+constexpr int TC_MMA_WARP = 4, TC_TMA_WARP = 5;
+constexpr int TC_THREADS = 6 * 32;
+constexpr uint32_t TMEM_COLS = 512;            // S x 2 (64 each) + O (256)
+constexpr float RESCALE_THRESHOLD = 8.0f;      // log2 units: rescale O only past 2^8
+
+struct __align__(1024) TcSmem {
+  uint16_t q[ROWS * HD];            // [col block 4][row 128][128 B], swizzled
+  uint16_t k[PSTAGES][PAGE * HD];   // [col block 4][pos 64][128 B]
+  uint16_t v[PSTAGES][PAGE * HD];
+  uint16_t p[ROWS * PAGE];          // [row 128][128 B], swizzled
+  uint64_t full[PSTAGES], empty[PSTAGES];
+  uint64_t s_full[2], s_free[2], p_full, o_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    attn_prefill_tc_kernel(const AttnPrefillArgs a, const __grid_constant__ CUtensorMap tmk,
+                           const __grid_constant__ CUtensorMap tmv) {
   extern __shared__ unsigned char raw[];
-  PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>((reinterpret_cast<uintptr_t>(raw) + 1023) &
-                                                    ~uintptr_t(1023));
+  TcSmem& sm = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(raw) + 1023) &
+                                          ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kvh = blockIdx.y, split = blockIdx.x;
-  const int end = a.pos0 + a.T;                     // positions [0, end) exist
+  const int end = a.pos0 + a.T;
   const int n_pages = (end + PAGE - 1) / PAGE;
   const int per = (n_pages + a.n_split - 1) / a.n_split;
   const int pg0 = split * per, pg1 = min(n_pages, pg0 + per);
-  float* rec = a.rec + ((int64_t)kvh * a.n_split + split) * ROWS * (HD + 2);
+  const int nt = max(0, pg1 - pg0);
+  float* rec = a.rec + ((int64_t)kvh * a.n_split + split) * ROWS * REC;
 
   if (tid == 0) {
     for (int s = 0; s < PSTAGES; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], PCONS);
+      mbar_init(&sm.empty[s], 1);
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.s_full[b], 1);
+      mbar_init(&sm.s_free[b], 1);
+    }
+    mbar_init(&sm.p_full, 1);
+    mbar_init(&sm.o_done, 1);
+    sm.abort = 0;
     fence_mbar_init();
   }
-  // q tile of this kv-head into shared memory, swizzled; rows of tokens
-  // beyond the chunk are zero
-  for (int i = tid; i < ROWS * (HD / 8); i += PTHREADS) {
+  if (warp == TC_MMA_WARP) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&sm.tmem_base)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  // q tile of this kv-head, swizzled; rows of tokens beyond the chunk are zero
+  for (int i = tid; i < ROWS * (HD / 8); i += TC_THREADS) {
     const int row = i / (HD / 8), ch = i % (HD / 8);
     uint4 w = make_uint4(0, 0, 0, 0);
     if ((row % TMAX) < a.T)
       w = *reinterpret_cast<const uint4*>(a.q_buf + ((int64_t)kvh * ROWS + row) * HD + ch * 8);
     *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(sm.q) + pswz(row, ch * 8, ROWS)) = w;
   }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const uint32_t t_s[2] = {tmem, tmem + 64}, t_o = tmem + 128;
 
-  if (warp == PCONS) {  // ---------------------------------------- producer
-    if (lane != 0) return;
-    for (int pg = pg0, i = 0; pg < pg1; ++pg, ++i) {
-      const int s = i % PSTAGES;
-      if (i >= PSTAGES && !mbar_wait(&sm.empty[s], ((i / PSTAGES) - 1) & 1, a.err)) return;
-      const int pid = a.page_row[pg];
-      const int rows = min(PAGE, end - pg * PAGE);
-      const int nbox = (pid >= 0 && pid < a.max_pages) ? (rows + BOX_ROWS - 1) / BOX_ROWS : 0;
-      if (nbox == 0) record_error(a.err, QC_ERR_BOUNDS);
-      mbar_arrive_expect_tx(&sm.full[s], uint32_t(nbox * 4 * BOX_BYTES * 2));
-      const int row0 = (pid * 4 + kvh) * PAGE;
-      for (int rb = 0; rb < nbox; ++rb)
-        for (int cb = 0; cb < 4; ++cb) {
-          const int off = (cb * PAGE * 128 + rb * BOX_BYTES) / 2;
-          tma2d(&sm.k[s][off], &tmk, cb * 64, row0 + rb * BOX_ROWS, &sm.full[s]);
-          tma2d(&sm.v[s][off], &tmv, cb * 64, row0 + rb * BOX_ROWS, &sm.full[s]);
+  if (warp == TC_TMA_WARP) {  // --------------------------------- producer
+    if (lane == 0) {
+      for (int i = 0; i < nt && !sm.abort; ++i) {
+        const int s = i % PSTAGES, pg = pg0 + i;
+        if (i >= PSTAGES && !mbar_wait(&sm.empty[s], ((i / PSTAGES) - 1) & 1, a.err)) {
+          sm.abort = 1;
+          break;
         }
-    }
-    return;
-  }
-
-  // ------------------------------------------------------------ consumers
-  const int g = lane >> 2, t4 = lane & 3;
-  const int r0 = warp * 16;                 // rows r0..r0+15 = head (r0 / 32), tokens
-  const int tok_a = (r0 % TMAX) + g;        // token of accumulator rows g (c0, c1)
-  const int tok_b = tok_a + 8;              // and g + 8 (c2, c3)
-  float o[32][4];
-#pragma unroll
-  for (int n = 0; n < 32; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
-  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
-  bool aborted = false;
-  const uint32_t qbase = smem_u32(sm.q);
-  for (int pg = pg0, i = 0; pg < pg1; ++pg, ++i) {
-    const int s = i % PSTAGES;
-    if (!aborted && !mbar_wait(&sm.full[s], (i / PSTAGES) & 1, a.err)) aborted = true;
-    if (aborted) continue;
-    const uint32_t kb = smem_u32(sm.k[s]), vb = smem_u32(sm.v[s]);
-    const int rows = min(PAGE, end - pg * PAGE);
-    // ---- S[16 rows x 64 pos] = Q . K^T
-    float sc[8][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.0f;
-#pragma unroll 4
-    for (int j = 0; j < 16; ++j) {
-      uint32_t af[4];
-      ldsm4(qbase + pswz(r0 + (lane & 7) + ((lane >> 3) & 1) * 8, 16 * j + (lane >> 4) * 8, ROWS),
-            af);
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {  // n-tiles 2np, 2np + 1
-        uint32_t bf[4];
-        ldsm4(kb + pswz(16 * np + (lane & 7) + (lane >> 4) * 8, 16 * j + ((lane >> 3) & 1) * 8,
-                        PAGE),
-              bf);
-        mma16816(sc[2 * np], af, bf[0], bf[1]);
-        mma16816(sc[2 * np + 1], af, bf[2], bf[3]);
+        const int pid = a.page_row[pg];
+        const int rows = min(PAGE, end - pg * PAGE);
+        // all 64 rows of a valid page: the P.V product reads every row of the
+        // tile (P is zero past `rows`), so none may be stale shared memory;
+        // pool rows are zeroed at creation or hold finite older tokens
+        const int nbox = (pid >= 0 && pid < a.max_pages) ? PAGE / BOX_ROWS : 0;
+        if (nbox == 0) record_error(a.err, QC_ERR_BOUNDS);
+        (void)rows;
+        mbar_arrive_expect_tx(&sm.full[s], uint32_t(nbox * 4 * BOX_BYTES * 2));
+        const int row0 = (pid * 4 + kvh) * PAGE;
+        for (int rb = 0; rb < nbox; ++rb)
+          for (int cb = 0; cb < 4; ++cb) {
+            const int off = (cb * PAGE * 128 + rb * BOX_BYTES) / 2;
+            tma2d(&sm.k[s][off], &tmk, cb * 64, row0 + rb * BOX_ROWS, &sm.full[s]);
+            tma2d(&sm.v[s][off], &tmv, cb * 64, row0 + rb * BOX_ROWS, &sm.full[s]);
+          }
       }
     }
-    // ---- mask (position exists, causal inside the chunk) and online softmax
-    const int base = pg * PAGE;
-    float mx_a = -INFINITY, mx_b = -INFINITY;
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int kp = base + n * 8 + 2 * t4 + e, col = n * 8 + 2 * t4 + e;
-        const bool va = col < rows && kp <= a.pos0 + tok_a && tok_a < a.T;
-        const bool vb2 = col < rows && kp <= a.pos0 + tok_b && tok_b < a.T;
-        sc[n][e] = va ? sc[n][e] * SCALE_LOG2 : -INFINITY;
-        sc[n][2 + e] = vb2 ? sc[n][2 + e] * SCALE_LOG2 : -INFINITY;
-        mx_a = fmaxf(mx_a, sc[n][e]);
-        mx_b = fmaxf(mx_b, sc[n][2 + e]);
-      }
-    mx_a = fmaxf(mx_a, __shfl_xor_sync(FULL_MASK, mx_a, 1));
-    mx_a = fmaxf(mx_a, __shfl_xor_sync(FULL_MASK, mx_a, 2));
-    mx_b = fmaxf(mx_b, __shfl_xor_sync(FULL_MASK, mx_b, 1));
-    mx_b = fmaxf(mx_b, __shfl_xor_sync(FULL_MASK, mx_b, 2));
-    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-    const float c_a = (mn_a == -INFINITY) ? 1.0f : exp2f(m_a - mn_a);
-    const float c_b = (mn_b == -INFINITY) ? 1.0f : exp2f(m_b - mn_b);
-    m_a = mn_a;
-    m_b = mn_b;
-    float ps_a = 0.0f, ps_b = 0.0f;
-    uint32_t pa[4][4];  // A fragments of P for the 4 k-steps of 16 positions
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      const float p0 = (sc[n][0] == -INFINITY) ? 0.0f : exp2f(sc[n][0] - mn_a);
-      const float p1 = (sc[n][1] == -INFINITY) ? 0.0f : exp2f(sc[n][1] - mn_a);
-      const float p2 = (sc[n][2] == -INFINITY) ? 0.0f : exp2f(sc[n][2] - mn_b);
-      const float p3 = (sc[n][3] == -INFINITY) ? 0.0f : exp2f(sc[n][3] - mn_b);
-      ps_a += p0 + p1;
-      ps_b += p2 + p3;
-      // k-step n/2: a0/a1 from the even n-tile, a2/a3 from the odd one
-      pa[n >> 1][(n & 1) * 2 + 0] = pack2(p0, p1);
-      pa[n >> 1][(n & 1) * 2 + 1] = pack2(p2, p3);
-    }
-    l_a = fmaf(l_a, c_a, ps_a);
-    l_b = fmaf(l_b, c_b, ps_b);
-#pragma unroll
-    for (int n = 0; n < 32; ++n) {
-      o[n][0] *= c_a; o[n][1] *= c_a;
-      o[n][2] *= c_b; o[n][3] *= c_b;
-    }
-    // ---- O[16 x 256] += P[16 x 64] . V[64 x 256]
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-      for (int dp = 0; dp < 16; ++dp) {  // n-tiles 2dp, 2dp + 1 (dims 16dp..16dp+15)
-        uint32_t bf[4];
-        ldsm4t(vb + pswz(16 * kk + (lane & 7) + ((lane >> 3) & 1) * 8, 16 * dp + (lane >> 4) * 8,
-                         PAGE),
-               bf);
-        mma16816(o[2 * dp], pa[kk], bf[0], bf[1]);
-        mma16816(o[2 * dp + 1], pa[kk], bf[2], bf[3]);
+  } else if (warp == TC_MMA_WARP) {  // ------------------------- MMA issuer
+    if (lane == 0) {
+      // S = Q . K^T: M 128, N 64, K-major A and B
+      const uint32_t id_s = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) |
+                            ((uint32_t(ROWS) >> 4) << 24);
+      // O += P . V: M 128, N 256, A K-major, B (V [pos][dim]) MN-major
+      const uint32_t id_o = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((256u >> 3) << 17) |
+                            ((uint32_t(ROWS) >> 4) << 24);
+      const uint32_t q_addr = smem_u32(sm.q), p_addr = smem_u32(sm.p);
+      for (int i = 0; i < nt; ++i) {
+        const int s = i % PSTAGES, b = i & 1;
+        if (!mbar_wait(&sm.full[s], (i / PSTAGES) & 1, a.err)) break;
+        if (i >= 2 && !mbar_wait(&sm.s_free[b], ((i >> 1) - 1) & 1, a.err)) break;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sm.k[s]), v_addr = smem_u32(sm.v[s]);
+        for (int cb = 0; cb < 4; ++cb)
+          for (int ks = 0; ks < 4; ++ks)
+            umma(t_s[b], umma_desc(q_addr + cb * ROWS * 128 + ks * 32, 16, 1024),
+                 umma_desc(k_addr + cb * PAGE * 128 + ks * 32, 16, 1024), id_s, (cb | ks) != 0);
+        umma_commit(&sm.s_full[b]);
+        if (!mbar_wait(&sm.p_full, i & 1, a.err)) break;   // softmax wrote P (and rescaled O)
+        tc_fence_after();
+        for (int kk = 0; kk < 4; ++kk)
+          umma(t_o, umma_desc(p_addr + kk * 32, 16, 1024),
+               umma_desc(v_addr + kk * 2048, PAGE * 128, 1024), id_o, (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&sm.o_done);
+        umma_commit(&sm.empty[s]);
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.empty[s]);
-  }
-  // ---- records: m (log2 domain), l, o unnormalised, per row
-  l_a += __shfl_xor_sync(FULL_MASK, l_a, 1);
-  l_a += __shfl_xor_sync(FULL_MASK, l_a, 2);
-  l_b += __shfl_xor_sync(FULL_MASK, l_b, 1);
-  l_b += __shfl_xor_sync(FULL_MASK, l_b, 2);
-  float* ra = rec + (int64_t)(r0 + g) * (HD + 2);
-  float* rb = rec + (int64_t)(r0 + g + 8) * (HD + 2);
-  if (t4 == 0) {
-    ra[0] = m_a; ra[1] = l_a;
-    rb[0] = m_b; rb[1] = l_b;
-  }
+  } else {  // ------------------------------------ softmax: thread = row
+    const int row = warp * 32 + lane, tok = row % TMAX;
+    const uint32_t lane_off = uint32_t(warp * 32) << 16;
+    float m_ref = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int i = 0; i < nt && ok; ++i) {
+      const int b = i & 1, pg = pg0 + i;
+      const int rows = min(PAGE, end - pg * PAGE);
+      ok = mbar_wait(&sm.s_full[b], (i >> 1) & 1, a.err);
+      if (!ok) break;
+      tc_fence_after();
+      float sv[64];
+      float (&s0)[32] = *reinterpret_cast<float(*)[32]>(&sv[0]);
+      float (&s1)[32] = *reinterpret_cast<float(*)[32]>(&sv[32]);
+      tmem_ld32(t_s[b] + lane_off, s0);
+      tmem_ld32(t_s[b] + lane_off + 32, s1);
+      tc_fence_before();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (row == 0) mbar_arrive(&sm.s_free[b]);
+      // mask (position exists; causal inside the chunk) and scale
+      float mt = -INFINITY;
 #pragma unroll
-  for (int n = 0; n < 32; ++n) {
-    const int d = n * 8 + 2 * t4;
-    ra[2 + d] = o[n][0];
-    ra[3 + d] = o[n][1];
-    rb[2 + d] = o[n][2];
-    rb[3 + d] = o[n][3];
+      for (int j = 0; j < 64; ++j) {
+        const int kp = pg * PAGE + j;
+        const bool valid = j < rows && kp <= a.pos0 + tok && tok < a.T;
+        sv[j] = valid ? sv[j] * SCALE_LOG2 : -INFINITY;
+        mt = fmaxf(mt, sv[j]);
+      }
+      // the previous P . V must be done before P is rewritten or O rescaled
+      if (i > 0) {
+        ok = mbar_wait(&sm.o_done, (i - 1) & 1, a.err);
+        if (!ok) break;
+        tc_fence_after();
+      }
+      if (mt > m_ref + RESCALE_THRESHOLD || (m_ref == -INFINITY && mt != -INFINITY)) {
+        const float f = (m_ref == -INFINITY) ? 0.0f : exp2f(m_ref - mt);
+        if (i > 0) {
+#pragma unroll 1
+          for (int c = 0; c < 256; c += 32) {
+            float ov[32];
+            tmem_ld32(t_o + lane_off + c, ov);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) ov[j] *= f;
+            tmem_st32(t_o + lane_off + c, ov);
+          }
+        }
+        l *= f;
+        m_ref = mt;
+      }
+      // P = 2^(s - m_ref) in bf16, row-major 128 B per row, swizzled
+      unsigned char* prow = reinterpret_cast<unsigned char*>(sm.p);
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        float pv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float x = sv[ch * 8 + e];
+          pv[e] = (x == -INFINITY) ? 0.0f : exp2f(x - m_ref);
+          l += pv[e];
+        }
+        uint4 w;
+        w.x = pack2(pv[0], pv[1]);
+        w.y = pack2(pv[2], pv[3]);
+        w.z = pack2(pv[4], pv[5]);
+        w.w = pack2(pv[6], pv[7]);
+        *reinterpret_cast<uint4*>(prow + row * 128 + ((ch ^ (row & 7)) << 4)) = w;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (row == 0) mbar_arrive(&sm.p_full);
+    }
+    // ---- record of this row: m (log2 domain), l, o unnormalised
+    if (ok && nt > 0) ok = mbar_wait(&sm.o_done, (nt - 1) & 1, a.err);
+    float* r = rec + (int64_t)row * REC;
+    if (ok && nt > 0) {
+      tc_fence_after();
+      r[0] = m_ref;
+      r[1] = l;
+#pragma unroll 1
+      for (int c = 0; c < 256; c += 32) {
+        float ov[32];
+        tmem_ld32(t_o + lane_off + c, ov);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          *reinterpret_cast<float4*>(r + 4 + c + j) = make_float4(ov[j], ov[j + 1], ov[j + 2], ov[j + 3]);
+      }
+    } else {
+      r[0] = -INFINITY;
+      r[1] = 0.0f;
+      for (int c = 0; c < 256; c += 4) *reinterpret_cast<float4*>(r + 4 + c) = make_float4(0, 0, 0, 0);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == TC_MMA_WARP) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
   }
 }
 
@@ -475,13 +563,13 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(const AttnPrefillA
   if (t >= a.T) return;
   float M = -INFINITY;
   for (int sp = 0; sp < a.n_split; ++sp)
-    M = fmaxf(M, a.rec[(((int64_t)kvh * a.n_split + sp) * ROWS + row) * (HD + 2)]);
+    M = fmaxf(M, a.rec[(((int64_t)kvh * a.n_split + sp) * ROWS + row) * REC]);
   float L = 0.0f, O = 0.0f;
   for (int sp = 0; sp < a.n_split; ++sp) {
-    const float* r = a.rec + (((int64_t)kvh * a.n_split + sp) * ROWS + row) * (HD + 2);
+    const float* r = a.rec + (((int64_t)kvh * a.n_split + sp) * ROWS + row) * REC;
     const float f = (r[0] == -INFINITY) ? 0.0f : exp2f(r[0] - M);
     L = fmaf(f, r[1], L);
-    O = fmaf(f, r[2 + d], O);
+    O = fmaf(f, r[4 + d], O);
   }
   const int h = kvh * 4 + hh;
   const float gt = bf2f(a.proj[(int64_t)t * 10240 + h * 2 * HD + HD + d]);
@@ -524,7 +612,7 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs& a, cudaStream_t s) {
 
 namespace qc {
 
-int attn_prefill_smem_bytes() { return (int)sizeof(PrefillSmem) + 1024; }
+int attn_prefill_smem_bytes() { return (int)sizeof(TcSmem) + 1024; }
 
 cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, const CUtensorMap& tmk,
                                 const CUtensorMap& tmv, cudaStream_t s) {
@@ -533,7 +621,7 @@ cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, const CUtensorMap& tmk
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel,
+    cudaError_t e = cudaFuncSetAttribute(attn_prefill_tc_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          attn_prefill_smem_bytes());
     if (e != cudaSuccess) return e;
@@ -542,7 +630,7 @@ cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, const CUtensorMap& tmk
   prefill_qk_kernel<<<a.T, 640, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  attn_prefill_kernel<<<dim3(a.n_split, 4), PTHREADS, attn_prefill_smem_bytes(), s>>>(a, tmk, tmv);
+  attn_prefill_tc_kernel<<<dim3(a.n_split, 4), TC_THREADS, attn_prefill_smem_bytes(), s>>>(a, tmk, tmv);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   prefill_combine_kernel<<<dim3(ROWS, 4), 256, 0, s>>>(a);
   return cudaGetLastError();

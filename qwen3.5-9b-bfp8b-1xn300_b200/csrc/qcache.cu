@@ -93,7 +93,7 @@ struct qc_ctx {
   int32_t job_cap = 0;
   int* dev_err = nullptr;
   uint16_t* pf_q = nullptr;     // prefill: q tile [4][128][256] bf16
-  float* pf_rec = nullptr;      // prefill: records [4][pf_split][128][258] f32
+  float* pf_rec = nullptr;      // prefill: records [4][pf_split][128][260] f32
   int32_t pf_split = 0;
   std::vector<CUtensorMap> tm_k, tm_v;  // per attention layer, for the TMA tile loads
 
@@ -367,13 +367,18 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
       {(void**)&c->chunk_start, (size_t)(c->job_cap + 1) * 8, "chunk_start"},
       {(void**)&c->dev_err, 16, "dev_err"},
       {(void**)&c->pf_q, (size_t)4 * 4 * QC_PREFILL_CHUNK * HD * 2, "prefill q"},
-      {(void**)&c->pf_rec, (size_t)4 * c->pf_split * 4 * QC_PREFILL_CHUNK * (HD + 2) * 4,
+      {(void**)&c->pf_rec, (size_t)4 * c->pf_split * 4 * QC_PREFILL_CHUNK * (HD + 4) * 4,
        "prefill records"},
   };
   for (const A& a : allocs) {
     e = cudaMalloc(a.p, a.bytes);
     if (e != cudaSuccess) return cuda_fail(e, a.what);
   }
+  // zeroed pools: rows past a page's valid length may enter a tensor-core
+  // product multiplied by zero, so they must never hold NaN bit patterns
+  if ((e = cudaMemset(c->k_pool, 0, (size_t)pool * 2)) ||
+      (e = cudaMemset(c->v_pool, 0, (size_t)pool * 2)))
+    return cuda_fail(e, "cudaMemset");
   // zeroed state so that a fresh sequence equals reset_state()
   if ((e = cudaMemset(c->state, 0, (size_t)cfg->max_seqs * std::max(ng, 1) * QC_GDN_STATE * 4)) ||
       (e = cudaMemset(c->ring, 0, (size_t)cfg->max_seqs * std::max(ng, 1) * RING_ELEMS * 2)) ||
@@ -875,7 +880,9 @@ int qc_attn_prefill(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, q
   a.pos0 = c->p_pos0;
   a.T = c->p_n;
   const int32_t n_pages = (c->p_pos0 + c->p_n + PAGE - 1) / PAGE;
-  a.n_split = std::min(c->pf_split, n_pages);
+  // at least 4 pages per CTA: each CTA's fixed cost (tensor-memory setup, the
+  // 64 KiB q tile, a 133 KB record) must be spread over several tiles
+  a.n_split = std::max(1, std::min(c->pf_split, n_pages / 4));
   a.err = c->dev_err;
   QC_CUDA(c, qc::launch_attn_prefill(a, c->tm_k[layer], c->tm_v[layer], (cudaStream_t)stream));
   return QC_OK;
