@@ -878,6 +878,10 @@ def main():
         cus, cores, sample, _, _ = cpu_baseline()
         line["cpu_baseline"] = {"value": round(cus, 3), "unit": "us/token/layer", "cores": cores,
                                 "kind": "port", "sample": sample}
+        # the reference's own thread count: its WorkerPool (src/engine.cpp:1631)
+        cus4, _, sample4, _, _ = cpu_baseline(budget_s=6.0, threads=4)
+        line["cpu_baseline_4_threads"] = {"value": round(cus4, 3), "unit": "us/token/layer",
+                                          "cores": 4, "kind": "port", "sample": sample4}
     emit(line)
     if dist is not None:
         dist.destroy_process_group()

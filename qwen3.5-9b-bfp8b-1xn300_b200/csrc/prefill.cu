@@ -342,9 +342,11 @@ struct __align__(1024) TcSmem {
   uint16_t q[ROWS * HD];            // [col block 4][row 128][128 B], swizzled
   uint16_t k[PSTAGES][PAGE * HD];   // [col block 4][pos 64][128 B]
   uint16_t v[PSTAGES][PAGE * HD];
-  uint16_t p[ROWS * PAGE];          // [row 128][128 B], swizzled
+  uint16_t p[2][ROWS * PAGE];       // double-buffered [row 128][128 B], swizzled
   uint64_t full[PSTAGES], empty[PSTAGES];
-  uint64_t s_full[2], s_free[2], p_full, o_done;
+  // per tile parity b: s_* for the S buffers, p_full[b] (P written), o_done[b]
+  // (P . V done); parity waits then never face a barrier two phases ahead
+  uint64_t s_full[2], s_free[2], p_full[2], o_done[2];
   uint32_t tmem_base;
   int abort;
 };
@@ -373,8 +375,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&sm.s_full[b], 1);
       mbar_init(&sm.s_free[b], 1);
     }
-    mbar_init(&sm.p_full, 1);
-    mbar_init(&sm.o_done, 1);
+    mbar_init(&sm.p_full[0], 1);
+    mbar_init(&sm.p_full[1], 1);
+    mbar_init(&sm.o_done[0], 1);
+    mbar_init(&sm.o_done[1], 1);
     sm.abort = 0;
     fence_mbar_init();
   }
@@ -433,24 +437,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // O += P . V: M 128, N 256, A K-major, B (V [pos][dim]) MN-major
       const uint32_t id_o = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((256u >> 3) << 17) |
                             ((uint32_t(ROWS) >> 4) << 24);
-      const uint32_t q_addr = smem_u32(sm.q), p_addr = smem_u32(sm.p);
-      for (int i = 0; i < nt; ++i) {
+      const uint32_t q_addr = smem_u32(sm.q);
+      // S(i) = Q . K(i)^T into TMEM buffer i & 1
+      auto issue_qk = [&](int i) -> bool {
         const int s = i % PSTAGES, b = i & 1;
-        if (!mbar_wait(&sm.full[s], (i / PSTAGES) & 1, a.err)) break;
-        if (i >= 2 && !mbar_wait(&sm.s_free[b], ((i >> 1) - 1) & 1, a.err)) break;
+        if (!mbar_wait(&sm.full[s], (i / PSTAGES) & 1, a.err)) return false;
+        if (i >= 2 && !mbar_wait(&sm.s_free[b], ((i >> 1) - 1) & 1, a.err)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sm.k[s]), v_addr = smem_u32(sm.v[s]);
+        const uint32_t k_addr = smem_u32(sm.k[s]);
         for (int cb = 0; cb < 4; ++cb)
           for (int ks = 0; ks < 4; ++ks)
             umma(t_s[b], umma_desc(q_addr + cb * ROWS * 128 + ks * 32, 16, 1024),
                  umma_desc(k_addr + cb * PAGE * 128 + ks * 32, 16, 1024), id_s, (cb | ks) != 0);
         umma_commit(&sm.s_full[b]);
-        if (!mbar_wait(&sm.p_full, i & 1, a.err)) break;   // softmax wrote P (and rescaled O)
+        return true;
+      };
+      bool ok = nt == 0 || issue_qk(0);
+      for (int i = 0; i < nt && ok; ++i) {
+        // the next tile's scores run while the softmax works on this one
+        if (i + 1 < nt && !(ok = issue_qk(i + 1))) break;
+        if (!mbar_wait(&sm.p_full[i & 1], (i >> 1) & 1, a.err)) break;   // softmax wrote P(i)
         tc_fence_after();
+        const int s = i % PSTAGES;
+        const uint32_t v_addr = smem_u32(sm.v[s]), p_addr = smem_u32(sm.p[i & 1]);
         for (int kk = 0; kk < 4; ++kk)
           umma(t_o, umma_desc(p_addr + kk * 32, 16, 1024),
                umma_desc(v_addr + kk * 2048, PAGE * 128, 1024), id_o, (i > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&sm.o_done);
+        umma_commit(&sm.o_done[i & 1]);
         umma_commit(&sm.empty[s]);
       }
     }
@@ -482,13 +495,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         sv[j] = valid ? sv[j] * SCALE_LOG2 : -INFINITY;
         mt = fmaxf(mt, sv[j]);
       }
-      // the previous P . V must be done before P is rewritten or O rescaled
-      if (i > 0) {
-        ok = mbar_wait(&sm.o_done, (i - 1) & 1, a.err);
-        if (!ok) break;
-        tc_fence_after();
-      }
-      if (mt > m_ref + RESCALE_THRESHOLD || (m_ref == -INFINITY && mt != -INFINITY)) {
+      // P buffer i & 1 was read by P . V of tile i - 2; O is complete up to
+      // tile i - 1 only after that product, which a rescale must wait for.
+      // Each o_done barrier completes once per tile of its parity, and the
+      // phase waited for is always the newest it can have completed (P(i)
+      // is not written yet), so parity waits are unambiguous.
+      const bool rescale =
+          mt > m_ref + RESCALE_THRESHOLD || (m_ref == -INFINITY && mt != -INFINITY);
+      if (i >= 2) ok = mbar_wait(&sm.o_done[i & 1], ((i - 2) >> 1) & 1, a.err);
+      if (ok && rescale && i >= 1) ok = mbar_wait(&sm.o_done[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err);
+      if (!ok) break;
+      tc_fence_after();
+      if (rescale) {
         const float f = (m_ref == -INFINITY) ? 0.0f : exp2f(m_ref - mt);
         if (i > 0) {
 #pragma unroll 1
@@ -504,7 +522,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         m_ref = mt;
       }
       // P = 2^(s - m_ref) in bf16, row-major 128 B per row, swizzled
-      unsigned char* prow = reinterpret_cast<unsigned char*>(sm.p);
+      unsigned char* prow = reinterpret_cast<unsigned char*>(sm.p[i & 1]);
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         float pv[8];
@@ -524,10 +542,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (row == 0) mbar_arrive(&sm.p_full);
+      if (row == 0) mbar_arrive(&sm.p_full[i & 1]);
     }
     // ---- record of this row: m (log2 domain), l, o unnormalised
-    if (ok && nt > 0) ok = mbar_wait(&sm.o_done, (nt - 1) & 1, a.err);
+    for (int k = max(0, nt - 2); k < nt && ok; ++k) ok = mbar_wait(&sm.o_done[k & 1], (k >> 1) & 1, a.err);
     float* r = rec + (int64_t)row * REC;
     if (ok && nt > 0) {
       tc_fence_after();
