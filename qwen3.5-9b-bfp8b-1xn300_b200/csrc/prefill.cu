@@ -80,6 +80,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArg
   // ---- phase A: conv + SiLU of q, k (all 128 channels) and of this CTA's v
   // channels, every token of the chunk (src/engine.cpp:3204-3234)
   constexpr int NCH = 2 * HK + GRB;
+#pragma unroll 4
   for (int idx = tid; idx < T * NCH; idx += 256) {
     const int t = idx / NCH, ch = idx % NCH;
     const int c = (ch < HK) ? kh * HK + ch
@@ -186,6 +187,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArg
     if (lane < GR) *cluster.map_shared_rank(&sm.ssq[r][t], lane) = ss;
   }
   cluster.sync();
+#pragma unroll 2
   for (int idx = tid; idx < T * GRB; idx += 256) {
     const int t = idx / GRB, d = idx % GRB;
     float tot = 0.0f;
@@ -388,13 +390,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                  "r"(TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
-  // q tile of this kv-head, swizzled; rows of tokens beyond the chunk are zero
-  for (int i = tid; i < ROWS * (HD / 8); i += TC_THREADS) {
-    const int row = i / (HD / 8), ch = i % (HD / 8);
-    uint4 w = make_uint4(0, 0, 0, 0);
-    if ((row % TMAX) < a.T)
-      w = *reinterpret_cast<const uint4*>(a.q_buf + ((int64_t)kvh * ROWS + row) * HD + ch * 8);
-    *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(sm.q) + pswz(row, ch * 8, ROWS)) = w;
+  // q tile of this kv-head, swizzled; rows of tokens beyond the chunk are zero.
+  // Loads are batched 8 deep so their L2 latencies overlap.
+  {
+    constexpr int N16 = ROWS * (HD / 8);   // 16-byte chunks
+    for (int i0 = tid; i0 < N16; i0 += 8 * TC_THREADS) {
+      uint4 w[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = i0 + k * TC_THREADS, row = i / (HD / 8), ch = i % (HD / 8);
+        w[k] = (i < N16 && (row % TMAX) < a.T)
+                   ? *reinterpret_cast<const uint4*>(a.q_buf + ((int64_t)kvh * ROWS + row) * HD + ch * 8)
+                   : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = i0 + k * TC_THREADS, row = i / (HD / 8), ch = i % (HD / 8);
+        if (i < N16)
+          *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(sm.q) + pswz(row, ch * 8, ROWS)) = w[k];
+      }
+    }
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   tc_fence_before();
