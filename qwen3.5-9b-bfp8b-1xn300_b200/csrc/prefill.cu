@@ -11,8 +11,10 @@
 // fp32 state in registers (2 rows per warp, one float4 per lane and row) and
 // runs the delta rule token after token — the state is read from and written
 // to HBM once per chunk instead of once per token.  Phase C applies
-// the gated RMSNorm per token.  The conv ring is advanced by a separate
-// launch after all heads have read it (gdn_prefill_ring_kernel).
+// the gated RMSNorm per token.
+//
+// The conv of all channels runs first in gdn_prefill_conv_kernel, which also
+// advances the conv ring.
 //
 // Attention: prefill_qk_kernel normalises and rotates the chunk's q (to a
 // bf16 scratch tile) and k, and appends K/V into the pages (the decode
@@ -71,14 +73,13 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArg
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int vh = blockIdx.x / GR, r = static_cast<int>(cluster.block_rank());
   const int kh = vh & 15;  // kh = vh % 16 (src/engine.cpp:3254)
-  const int T = a.T, pos0 = a.pos0;
-  const float* w = a.conv_w;
+  const int T = a.T;
   // first half of a split cluster barrier: peers may write our shared memory
   // after their matching wait
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
-  // ---- phase A: conv + SiLU of q, k (all 128 channels) and of this CTA's v
-  // channels, every token of the chunk (src/engine.cpp:3204-3234)
+  // ---- phase A: the chunk's conv outputs of the head's q and k channels and
+  // of this CTA's v channels (computed once per chunk by the conv kernel)
   constexpr int NCH = 2 * HK + GRB;
 #pragma unroll 4
   for (int idx = tid; idx < T * NCH; idx += 256) {
@@ -86,18 +87,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArg
     const int c = (ch < HK) ? kh * HK + ch
                 : (ch < 2 * HK) ? 2048 + kh * HK + (ch - HK)
                                 : 4096 + vh * HK + r * GRB + (ch - 2 * HK);
-    float xs[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int p = pos0 + t - 3 + j;  // tap j reads position p
-      xs[j] = (p >= pos0) ? bf2f(a.proj[(int64_t)(p - pos0) * 12352 + c])
-                          : bf2f(a.ring[(p & 3) * CONV + c]);
-    }
-    float y = xs[0] * w[c];
-    y = fmaf(xs[1], w[CONV + c], y);
-    y = fmaf(xs[2], w[2 * CONV + c], y);
-    y = fmaf(xs[3], w[3 * CONV + c], y);
-    y = silu_exact(y);
+    const float y = a.conv_out[(int64_t)t * CONV + c];
     if (ch < HK) sm.q[t][ch] = y;
     else if (ch < 2 * HK) sm.k[t][ch - HK] = y;
     else sm.v[t][ch - 2 * HK] = y;
@@ -201,16 +191,52 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArg
   }
 }
 
-// Advance the conv ring past the chunk: positions max(pos0, pos0 + T - 4) ..
-// pos0 + T - 1 land in slots position & 3 (the four most recent inputs).
-__global__ void gdn_prefill_ring_kernel(const GdnPrefillArgs a) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= CONV) return;
-  const int first = max(0, a.T - 4);
-  for (int t = first; t < a.T; ++t)
-    a.ring[((a.pos0 + t) & 3) * CONV + c] = a.proj[(int64_t)t * 12352 + c];
+// Conv + SiLU of every channel for every token of the chunk
+// (src/engine.cpp:3204-3234) into conv_out [T][8192] f32.  A CTA covers 32
+// channels x 4 groups of 8 tokens; a group's history is the conv ring (first
+// group) or the chunk's own earlier inputs.  After a CTA barrier — every read
+// of the ring for these channels happens inside this CTA — the threads owning
+// the chunk's last 4 tokens advance the ring (slot = position & 3).
+constexpr int CONV_CH = 32;
+constexpr int CONV_TG = 8;
+__global__ void __launch_bounds__(128) gdn_prefill_conv_kernel(const GdnPrefillArgs a) {
+  const int cl = threadIdx.x & 31, tg = threadIdx.x >> 5;
+  const int c = blockIdx.x * CONV_CH + cl;
+  const int pos0 = a.pos0, T = a.T, t0 = tg * CONV_TG;
+  const float w0 = a.conv_w[c], w1 = a.conv_w[CONV + c], w2 = a.conv_w[2 * CONV + c],
+              w3 = a.conv_w[3 * CONV + c];
+  // history h[j] = input at chunk-relative token t0 - 3 + j
+  float h[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int t = t0 - 3 + j;
+    h[j] = (t < 0) ? bf2f(a.ring[((pos0 + t) & 3) * CONV + c])
+                   : (t < T ? bf2f(a.proj[(int64_t)t * 12352 + c]) : 0.0f);
+  }
+  uint16_t xb[CONV_TG];
+#pragma unroll
+  for (int j = 0; j < CONV_TG; ++j)
+    xb[j] = (t0 + j < T) ? a.proj[(int64_t)(t0 + j) * 12352 + c] : uint16_t(0);
+#pragma unroll
+  for (int j = 0; j < CONV_TG; ++j) {
+    if (t0 + j >= T) break;
+    const float x = bf2f(xb[j]);
+    float y = h[0] * w0;
+    y = fmaf(h[1], w1, y);
+    y = fmaf(h[2], w2, y);
+    y = fmaf(x, w3, y);
+    a.conv_out[(int64_t)(t0 + j) * CONV + c] = silu_exact(y);
+    h[0] = h[1];
+    h[1] = h[2];
+    h[2] = x;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < CONV_TG; ++j) {
+    const int t = t0 + j;
+    if (t < T && t >= T - 4) a.ring[((pos0 + t) & 3) * CONV + c] = xb[j];
+  }
 }
-
 
 // ------------------------------------------------------------- attention
 
@@ -623,6 +649,9 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs& a, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     configured_device = dev;
   }
+  gdn_prefill_conv_kernel<<<CONV / CONV_CH, 32 * (TMAX / CONV_TG), 0, s>>>(a);
+  cudaError_t e0 = cudaGetLastError();
+  if (e0 != cudaSuccess) return e0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(32 * GR, 1, 1);
   cfg.blockDim = dim3(256, 1, 1);
@@ -635,10 +664,7 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs& a, cudaStream_t s) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gdn_prefill_kernel, a);
-  if (e != cudaSuccess) return e;
-  gdn_prefill_ring_kernel<<<CONV / 256, 256, 0, s>>>(a);
-  return cudaGetLastError();
+  return cudaLaunchKernelEx(&cfg, gdn_prefill_kernel, a);
 }
 
 }  // namespace qc

@@ -94,6 +94,7 @@ struct qc_ctx {
   int* dev_err = nullptr;
   uint16_t* pf_q = nullptr;     // prefill: q tile [4][128][256] bf16
   float* pf_rec = nullptr;      // prefill: records [4][pf_split][128][260] f32
+  float* pf_conv = nullptr;     // prefill: conv outputs [32][8192] f32
   int32_t pf_split = 0;
   std::vector<CUtensorMap> tm_k, tm_v;  // per attention layer, for the TMA tile loads
 
@@ -367,6 +368,7 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
       {(void**)&c->chunk_start, (size_t)(c->job_cap + 1) * 8, "chunk_start"},
       {(void**)&c->dev_err, 16, "dev_err"},
       {(void**)&c->pf_q, (size_t)4 * 4 * QC_PREFILL_CHUNK * HD * 2, "prefill q"},
+      {(void**)&c->pf_conv, (size_t)QC_PREFILL_CHUNK * QC_CONV_CH * 4, "prefill conv"},
       {(void**)&c->pf_rec, (size_t)4 * c->pf_split * 4 * QC_PREFILL_CHUNK * (HD + 4) * 4,
        "prefill records"},
   };
@@ -445,7 +447,7 @@ void qc_destroy(qc_ctx* c) {
     cudaDeviceSynchronize();
     void* ptrs[] = {c->k_pool, c->v_pool, c->state, c->ring, c->snap_state, c->snap_hist,
                     c->q_norm, c->k_norm, c->ssm_a, c->dt_bias, c->ssm_norm, c->conv_w,
-                    c->rope_cos, c->rope_sin, c->page_table, c->desc, c->desc_part, c->pf_q, c->pf_rec,
+                    c->rope_cos, c->rope_sin, c->page_table, c->desc, c->desc_part, c->pf_q, c->pf_rec, c->pf_conv,
                     c->part_m, c->part_l,
                     c->part_o, c->jobs, c->chunk_start, c->dev_err};
     for (void* p : ptrs)
@@ -902,6 +904,7 @@ int qc_gdn_prefill(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc
   g.ssm_a = c->ssm_a + layer * 32;
   g.dt_bias = c->dt_bias + layer * 32;
   g.ssm_norm = c->ssm_norm + layer * 128;
+  g.conv_out = c->pf_conv;
   g.pos0 = c->p_pos0;
   g.T = c->p_n;
   QC_CUDA(c, qc::launch_gdn_prefill(g, (cudaStream_t)stream));
