@@ -669,6 +669,122 @@ def run_prefill(args, prompt=2048):
     return res, prompt
 
 
+def gemv_shapes():
+    """The projection GEMVs around the cache path in one decode step, in layer
+    order: per DeltaNet layer the combined in-projection (12352 x 4096) and the
+    out-projection (4096 x 4096); per attention layer the QKV projection
+    (10240 x 4096) and the out-projection (4096 x 4096)."""
+    out = []
+    for l in range(N_LAYERS):
+        out.append((10240 if is_attn(l) else 12352, 4096))
+        out.append((4096, 4096))
+    return out
+
+
+def run_gemv(args, batches=(1, 8, 16)):
+    """BFP8_B projection GEMVs (include/qbfp8.h) of one decode step: 64
+    distinct matrices (2.2 GB of tiles, far above L2), captured once per batch
+    size in a CUDA graph.  Device time of the timed graph replays with CUDA
+    events, and e2e with the step's activations copied in from pinned host
+    memory and the outputs copied back inside the timed region."""
+    import torch
+    qc = load_pkg("qcache")
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    shapes = gemv_shapes()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    mats = []
+    for M, K in shapes:
+        w = (torch.randn(M, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        m = qc.Bfp8Matrix(M, K)
+        m.pack_bf16(w.data_ptr())
+        mats.append(m)
+        del w
+    torch.cuda.synchronize()
+    tile_bytes = sum(qc.Bfp8Matrix.packed_bytes(M, K) for M, K in shapes)
+    stream = torch.cuda.Stream()
+    res = {}
+    for B in batches:
+        xs = [torch.randn(B, K, generator=g, device="cuda").to(torch.bfloat16) for _, K in shapes]
+        ys = [torch.empty(B, M, device="cuda", dtype=torch.bfloat16) for M, _ in shapes]
+
+        def step(st):
+            for m, x, y in zip(mats, xs, ys):
+                m.gemv(x.data_ptr(), B, y.data_ptr(), st)
+        with torch.cuda.stream(stream):
+            step(stream.cuda_stream)
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step(stream.cuda_stream)
+            for _ in range(args.warmup):
+                graph.replay()
+            stream.synchronize()
+            clk = ClockSampler(torch.cuda.current_device()) if B == 1 else None
+            if clk:
+                clk.start()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+            stream.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            clocks = clk.stop() if clk else None
+            # one launch alone (the largest matrix), for the kernel roofline
+            big = max(range(len(shapes)), key=lambda i: shapes[i][0])
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 20
+            f0.record(stream)
+            for _ in range(reps):
+                mats[big].gemv(xs[big].data_ptr(), B, ys[big].data_ptr(), stream.cuda_stream)
+            f1.record(stream)
+            stream.synchronize()
+            one_ms = f0.elapsed_time(f1) / reps
+            # e2e: activations in from pinned host memory, outputs back out
+            hx = [torch.empty_like(x, device="cpu").pin_memory() for x in xs]
+            hy = [torch.empty_like(y, device="cpu").pin_memory() for y in ys]
+            stream.synchronize()
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for _ in range(args.steps):
+                for x, h in zip(xs, hx):
+                    x.copy_(h, non_blocking=True)
+                graph.replay()
+                for y, h in zip(ys, hy):
+                    h.copy_(y, non_blocking=True)
+            t1.record(stream)
+            stream.synchronize()
+            e2e_ms = t0.elapsed_time(t1) / args.steps
+        res[B] = dict(ms=ms, one_ms=one_ms, big=shapes[big], clocks=clocks, e2e_ms=e2e_ms,
+                      h2d=sum(x.numel() * 2 for x in xs), d2h=sum(y.numel() * 2 for y in ys))
+    for m in mats:
+        m.check()
+    return res, tile_bytes
+
+
+def gemv_cpu_baseline(budget_s=10.0, threads=None):
+    """The oracle's threaded BFP8_B GEMV (liboracle_fast.so) on a bounded sample:
+    repeated 12352 x 4096 GEMVs at batch 1, scaled to the 64-matrix step by
+    tile bytes.  Returns (us per step, threads, sample)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    synth = load_pkg("synth")
+    threads = threads or os.cpu_count() or 1
+    M, K = 12352, 4096
+    w = synth.bf16_bits(np.random.default_rng(1).standard_normal((M, K)).astype(np.float32) * 0.02)
+    packed = oracle.bfp8_pack(w)
+    x = synth.gemv_inputs(1, 1, K)
+    oracle.bfp8_gemv(packed, M, K, x, n_threads=threads, fast=True)
+    t0, reps = time.perf_counter(), 0
+    while time.perf_counter() - t0 < budget_s:
+        oracle.bfp8_gemv(packed, M, K, x, n_threads=threads, fast=True)
+        reps += 1
+    per = (time.perf_counter() - t0) / reps
+    step_bytes = sum((Mi // 32) * (Ki // 32) * 1088 for Mi, Ki in gemv_shapes())
+    return per * step_bytes / packed.size * 1e6, threads, f"{reps} GEMVs of 12352x4096 at batch 1"
+
+
 # ------------------------------------------------------------ CPU baseline
 
 
@@ -743,7 +859,7 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(WORKLOADS) + ["prefix", "prefill"],
+    ap.add_argument("--config", choices=sorted(WORKLOADS) + ["prefix", "prefill", "gemv"],
                     default="stack",
                     help="stack = the headline workload; the others are the baseline's "
                          "per-component configurations")
@@ -786,7 +902,43 @@ def main():
               "token_by_token_decode_ms": round(r["decode"], 3),
               "speedup_vs_token_by_token": round(r["decode"] / r["prefill"], 2)})
         return
-    if args.config in ("prefix", "prefill"):
+    if args.config == "gemv" and args.impl == "ours":
+        r, tile_bytes = run_gemv(args)
+        peak, peak_kind = measured_peaks()
+        b1 = r[1]
+        M, K = b1["big"]
+        one_bytes = (M // 32) * (K // 32) * 1088 + M * 2 + K * 2
+        k_gbs = one_bytes / (b1["one_ms"] * 1e-3) / 1e9
+        line = {"metric": "projection GEMV us/decode step", "value": round(b1["ms"] * 1e3, 2),
+                "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bfp8_b weights, bf16 activations, f32 accumulate",
+                "data": "synthetic (seeded random weights ~N(0, 0.02) packed on device)",
+                "config": {"workload": "the 64 BFP8_B projection GEMVs of one decode step of "
+                                       "the 32-layer stack (24 x 12352x4096 + 8 x 10240x4096 "
+                                       "in-projections, 32 x 4096x4096 out-projections), batch 1, "
+                                       "CUDA graph; 2.2 GB of tiles per step (inputs > L2)",
+                           "name": "gemv"},
+                "tile_bytes_per_step": tile_bytes,
+                "achieved_gbs": round(tile_bytes / (b1["ms"] * 1e-3) / 1e9, 1),
+                "batches": {str(B): {"us_per_step": round(v["ms"] * 1e3, 2),
+                                     "gbs": round(tile_bytes / (v["ms"] * 1e-3) / 1e9, 1)}
+                            for B, v in r.items()},
+                "roofline": {"kernel": f"bfp8_gemv_kernel ({M}x{K}, batch 1)", "bound": "hbm",
+                             "achieved": round(k_gbs, 1), "peak": peak, "peak_kind": peak_kind,
+                             "unit": "GB/s", "frac": round(k_gbs / peak, 4), "traffic": None,
+                             "algorithmic_bytes_per_launch": one_bytes},
+                "e2e": {"value": round(b1["e2e_ms"] * 1e3, 2), "unit": "us",
+                        "h2d_bytes_per_step": b1["h2d"], "d2h_bytes_per_step": b1["d2h"]},
+                "gpu_launches": args.steps * len(gemv_shapes()),
+                "clocks": b1["clocks"]}
+        if not args.no_cpu_baseline:
+            cus, cores, sample = gemv_cpu_baseline()
+            line["cpu_baseline"] = {"value": round(cus, 1), "unit": "us/decode step",
+                                    "cores": cores, "kind": "port", "sample": sample}
+        emit(line)
+        return
+    if args.config in ("prefix", "prefill", "gemv"):
         args.config = "stack"
     kinds, n_total, ctx, desc = WORKLOADS[args.config]
     if args.seqs:

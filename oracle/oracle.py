@@ -47,6 +47,13 @@ def lib(fast: bool = False) -> C.CDLL:
         "qo_gdn_decode_batch": (None, [I, P, P, P, P, P, P, P, P, I, I]),
         "qo_attn_decode_batch": (None, [I, P, P, P, P, P, P, C.c_int64, P, I, I]),
         "qo_prefix_decide": (I, [P, I, P, I, P]),
+        "qo_bfp8_packed_bytes": (C.c_int64, [I, I]),
+        "qo_bfp8_pack": (None, [P, I, I, P]),
+        "qo_bfp8_unpack": (None, [P, I, I, P]),
+        "qo_bfp8_gemv": (None, [P, I, I, P, I, I, P, P, I]),
+        "qo_exp_ref": (C.c_double, [C.c_double]),
+        "qo_sample_mass": (C.c_uint32, [C.c_float, C.c_float, C.c_float]),
+        "qo_sample": (C.c_int32, [P, I, C.c_float, C.c_float, C.c_double, P]),
     }
     for k, (r, a) in sig.items():
         f = getattr(L, k)
@@ -119,3 +126,43 @@ def prefix_decide(cached, prompt):
     reset = C.c_int()
     n = lib().qo_prefix_decide(_p(c), len(c), _p(p), len(p), C.byref(reset))
     return n, bool(reset.value)
+
+
+def bfp8_pack(w_bits: np.ndarray) -> np.ndarray:
+    """bf16 bits [M][K] -> BFP8_B tiles (uint8, GGUF type-200 layout)."""
+    w = np.ascontiguousarray(w_bits, np.uint16)
+    M, K = w.shape
+    out = np.zeros(lib().qo_bfp8_packed_bytes(M, K), np.uint8)
+    lib().qo_bfp8_pack(_p(w), M, K, _p(out))
+    return out
+
+
+def bfp8_unpack(packed: np.ndarray, M: int, K: int) -> np.ndarray:
+    w = np.zeros((M, K), np.float32)
+    lib().qo_bfp8_unpack(_p(np.ascontiguousarray(packed, np.uint8)), M, K, _p(w))
+    return w
+
+
+def bfp8_gemv(packed, M, K, x_bits, residual_bits=None, n_threads=1, fast=False):
+    """y = W x for x bf16 bits [B][K]; with residual_bits, the reference's
+    resadd rounding.  Returns (y bf16 bits [B][M], y32 f32 [B][M])."""
+    x = np.ascontiguousarray(x_bits, np.uint16).reshape(-1, K)
+    B = x.shape[0]
+    y = (np.zeros((B, M), np.uint16) if residual_bits is None
+         else np.array(residual_bits, np.uint16).reshape(B, M).copy())
+    y32 = np.zeros((B, M), np.float32)
+    lib(fast).qo_bfp8_gemv(_p(np.ascontiguousarray(packed, np.uint8)), M, K, _p(x), B,
+                           0 if residual_bits is None else 1, _p(y), _p(y32), n_threads)
+    return y, y32
+
+
+def sample(logits_bits, temperature, top_p=0.9, u=0.0):
+    """One row: (token, nucleus size) of the restated sample_token."""
+    lg = np.ascontiguousarray(logits_bits, np.uint16).reshape(-1)
+    kept = C.c_int32()
+    tok = lib().qo_sample(_p(lg), lg.size, temperature, top_p, float(u), C.byref(kept))
+    return tok, kept.value
+
+
+def exp_ref(x: float) -> float:
+    return lib().qo_exp_ref(float(x))

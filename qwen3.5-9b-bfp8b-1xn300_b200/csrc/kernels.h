@@ -90,6 +90,7 @@ struct GdnPrefillArgs {
   const float* ssm_a;
   const float* dt_bias;
   const float* ssm_norm;
+  float* conv_out;           // scratch [T][8192] f32: conv + SiLU outputs of the chunk
   int32_t pos0;              // position of the chunk's first token
   int32_t T;
 };
@@ -139,5 +140,46 @@ cudaError_t launch_copy_jobs(const CopyJob* jobs_dev, int32_t n_jobs, const int6
 // Conv ring <-> oldest-first [3][8192] history of one layer of one sequence.
 cudaError_t launch_ring_to_hist(const uint16_t* ring, int32_t pos, uint16_t* hist, cudaStream_t s);
 cudaError_t launch_hist_to_ring(const uint16_t* hist, int32_t pos, uint16_t* ring, cudaStream_t s);
+
+// BFP8_B GEMV (bfp8.cu).  Rows m < split go to y0[b * ld0 + m], the others to
+// y1[b * ld1 + m - split]; mode 1 adds into y0/y1 with the reference's resadd
+// rounding.  batch <= bfp8_gemv_columns() per launch; with S > 1 k-chunks a
+// merge kernel follows the GEMV on the stream.
+struct Bfp8GemvArgs {
+  const uint8_t* w;
+  const uint16_t* x;
+  uint16_t* y0;
+  uint16_t* y1;
+  int64_t ld0, ld1;
+  int32_t split;
+  int32_t mode;
+  float* partial;   // [S][columns][M] f32
+  const uint16_t* x16;  // [columns][K] f16 activations (scaled), written by the conversion
+  uint16_t* x16w;
+  const float* xscale;  // [columns] 2^-s of each activation row
+  float* xscalew;
+  int* err;
+  int32_t M, K, Mt, Kt, ku, S, n_units, batch;
+  int32_t diag;
+};
+cudaError_t bfp8_prepare_device();
+cudaError_t launch_bfp8_gemv(const Bfp8GemvArgs& a, int grid, cudaStream_t s);
+cudaError_t launch_bfp8_pack(const uint16_t* w, int32_t M, int32_t K, uint8_t* out, cudaStream_t s);
+cudaError_t launch_bfp8_transcode(uint8_t* tiles, int64_t n_tiles, int to_device, cudaStream_t s);
+int bfp8_gemv_columns();
+int bfp8_gemv_warps_per_cta();
+int bfp8_gemv_ctas_per_sm(int batch);
+
+// Token sampling (sample.cu): one cluster of CTAs per row of logits.
+struct SampleArgs {
+  const uint16_t* logits;  // [batch][ld] bf16
+  int64_t ld;
+  int32_t vocab, batch, slice;
+  float temperature, top_p;
+  const double* uniform;   // [batch] in [0, 1)
+  int32_t* tokens;         // [batch]
+};
+cudaError_t launch_sample(const SampleArgs& a, cudaStream_t s);
+size_t sample_smem_bytes();
 
 }  // namespace qc

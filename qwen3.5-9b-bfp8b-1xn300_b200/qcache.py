@@ -15,7 +15,7 @@ import re
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libqcache.so")
-HEADER = os.path.join(HERE, "..", "include", "qcache.h")
+HEADERS = [os.path.join(HERE, "..", "include", h) for h in ("qcache.h", "qbfp8.h", "qsample.h")]
 
 QC_OK, QC_ERR_ARG, QC_ERR_OOM, QC_ERR_CUDA, QC_ERR_TIMEOUT, QC_ERR_BOUNDS, QC_ERR_NODEVICE = range(7)
 DEVICE_NONE = -1
@@ -54,10 +54,13 @@ PI32 = C.POINTER(C.c_int32)
 
 
 def header_functions() -> list[str]:
-    """Names of every function include/qcache.h declares."""
-    with open(HEADER) as f:
-        text = f.read()
-    return sorted(set(re.findall(r"^\s*(?:int|void|const char\*)\s+(qc_\w+)\s*\(", text, re.M)))
+    """Names of every function the headers in include/ declare."""
+    text = ""
+    for h in HEADERS:
+        with open(h) as f:
+            text += f.read()
+    pat = r"^\s*(?:int64_t|int|void\s*\*|void|const char\*)\s*(qc_\w+)\s*\("
+    return sorted(set(re.findall(pat, text, re.M)))
 
 
 def lib() -> C.CDLL:
@@ -104,6 +107,18 @@ def lib() -> C.CDLL:
         "qc_attn_partial": (C.c_int, [P, C.c_int, P, P, P]),
         "qc_attn_combine": (C.c_int, [P, P, I32, P, P, P]),
         "qc_attn_decode_noalloc": (C.c_int, [P, P, P, I32, P, I32, PI32, I32, P, P, P, P, P, P]),
+        "qc_bfp8_packed_bytes": (C.c_int64, [I32, I32]),
+        "qc_bfp8_create": (C.c_int, [C.c_int, I32, I32, C.POINTER(P)]),
+        "qc_bfp8_destroy": (None, [P]),
+        "qc_bfp8_tiles": (P, [P]),
+        "qc_bfp8_upload": (C.c_int, [P, P, P]),
+        "qc_bfp8_download": (C.c_int, [P, P, P]),
+        "qc_bfp8_pack_bf16": (C.c_int, [P, P, P]),
+        "qc_bfp8_gemv": (C.c_int, [P, P, I32, P, P]),
+        "qc_bfp8_gemv_resadd": (C.c_int, [P, P, I32, P, P]),
+        "qc_bfp8_gemv_split": (C.c_int, [P, P, I32, I32, P, P, P]),
+        "qc_bfp8_check": (C.c_int, [P]),
+        "qc_sample": (C.c_int, [P, C.c_int64, I32, I32, C.c_float, C.c_float, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -303,5 +318,69 @@ def attn_decode_noalloc(proj_ptr, k_pool_ptr, v_pool_ptr, max_pages, page_table_
     rc = L.qc_attn_decode_noalloc(proj_ptr, k_pool_ptr, v_pool_ptr, max_pages, page_table_ptr,
                                   pt_stride, _i32arr(pos), len(pos), q_norm_ptr, k_norm_ptr,
                                   rope_cos_ptr, rope_sin_ptr, out_ptr, stream)
+    if rc:
+        raise QCacheError(rc, L.qc_last_error(None).decode())
+
+
+class Bfp8Matrix:
+    """One BFP8_B weight matrix on one GPU (include/qbfp8.h)."""
+
+    def __init__(self, M: int, K: int, device: int = 0):
+        self.M, self.K = M, K
+        self._m = P()
+        rc = lib().qc_bfp8_create(device, M, K, C.byref(self._m))
+        if rc:
+            raise QCacheError(rc, lib().qc_last_error(None).decode())
+
+    def close(self):
+        if self._m:
+            lib().qc_bfp8_destroy(self._m)
+            self._m = P()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _ck(self, rc):
+        if rc:
+            raise QCacheError(rc, lib().qc_last_error(None).decode())
+
+    @staticmethod
+    def packed_bytes(M: int, K: int) -> int:
+        return lib().qc_bfp8_packed_bytes(M, K)
+
+    @property
+    def tiles_ptr(self) -> int:
+        return lib().qc_bfp8_tiles(self._m)
+
+    def upload(self, host_ptr, stream=0):
+        self._ck(lib().qc_bfp8_upload(self._m, host_ptr, stream))
+
+    def download(self, host_ptr, stream=0):
+        self._ck(lib().qc_bfp8_download(self._m, host_ptr, stream))
+
+    def pack_bf16(self, w_ptr, stream=0):
+        self._ck(lib().qc_bfp8_pack_bf16(self._m, w_ptr, stream))
+
+    def gemv(self, x_ptr, batch, y_ptr, stream=0):
+        self._ck(lib().qc_bfp8_gemv(self._m, x_ptr, batch, y_ptr, stream))
+
+    def gemv_resadd(self, x_ptr, batch, residual_ptr, stream=0):
+        self._ck(lib().qc_bfp8_gemv_resadd(self._m, x_ptr, batch, residual_ptr, stream))
+
+    def gemv_split(self, x_ptr, batch, split_m, y0_ptr, y1_ptr, stream=0):
+        self._ck(lib().qc_bfp8_gemv_split(self._m, x_ptr, batch, split_m, y0_ptr, y1_ptr, stream))
+
+    def check(self):
+        self._ck(lib().qc_bfp8_check(self._m))
+
+
+def sample(logits_ptr, ld, vocab, batch, temperature, top_p, uniform_ptr, tokens_ptr, stream=0):
+    """qc_sample (include/qsample.h): one token per row of bf16 logits."""
+    L = lib()
+    rc = L.qc_sample(logits_ptr, ld, vocab, batch, temperature, top_p, uniform_ptr, tokens_ptr,
+                     stream)
     if rc:
         raise QCacheError(rc, L.qc_last_error(None).decode())

@@ -88,3 +88,26 @@ def gdn_inputs(seed: int, n_seq: int):
     hist = bf16_bits(normal(seed * 8 + 5, (n_seq, 3, 8192)))
     proj = bf16_bits(normal(seed * 8 + 6, (n_seq, 12352)))
     return dict(state=state, hist=hist, proj=proj)
+
+
+def bfp8_weights(seed: int, M: int, K: int, std: float = 0.02, edges: bool = True) -> np.ndarray:
+    """bf16 bits [M][K] ~ N(0, std).  With `edges`, the first tile-row carries
+    the format's edge cases: an all-zero face row, a face row whose values
+    span 2^-30 .. 1 (magnitudes that shift out), exact powers of two, values
+    that round up to the saturated magnitude, and negative zeros."""
+    w = normal(seed, (M, K), std=std).astype(np.float32)
+    if edges and M >= 32 and K >= 32:
+        w[0, :16] = 0.0
+        w[1, :16] = np.float32(2.0) ** -np.arange(0, 32, 2, dtype=np.float32)
+        w[1, 3::4] *= -1
+        w[2, :16] = [1.0, 0.5, -0.25, 0.125, 2.0, -4.0, 0.0, 1.0 / 64, 1.5, -1.5, 3.0, 0.75,
+                     -0.375, 1.0 / 128, 1.0 / 256, -1.0 / 512]
+        w[3, :16] = np.float32(1.9921875)  # bf16 0x3fff: rounds to 128 -> saturates
+        w[3, 8:16] = np.float32(-1.9921875)
+        w[4, 16:32] = -0.0
+    return bf16_bits(w)
+
+
+def gemv_inputs(seed: int, batch: int, K: int) -> np.ndarray:
+    """Activations bf16 bits [batch][K] ~ N(0, 1) (post-RMSNorm hidden rows)."""
+    return bf16_bits(normal(seed * 8 + 7, (batch, K)))

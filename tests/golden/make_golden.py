@@ -23,6 +23,7 @@ synth = load_pkg_module("synth")
 # (seed, cached positions): crosses 0, a page boundary, a full page, ragged
 ATTN_CASES = [(11, 0), (12, 63), (13, 64), (14, 130)]
 GDN_CASES = [(21, 0), (22, 5)]  # (seed, position of the token: ring phase)
+BFP8_CASES = [(31, 64, 128, 3), (32, 96, 64, 1)]  # (seed, M, K, batch)
 
 
 def attn_case(seed, ctx):
@@ -47,6 +48,16 @@ def gdn_case(seed, pos):
                 state_sample=state.reshape(-1)[::997].copy(), hist=hist, pos=np.int32(pos))
 
 
+def bfp8_case(seed, M, K, batch):
+    w = synth.bfp8_weights(seed, M, K)
+    packed = oracle.bfp8_pack(w)
+    x = synth.gemv_inputs(seed, batch, K)
+    y, y32 = oracle.bfp8_gemv(packed, M, K, x)
+    res = synth.bf16_bits(synth.normal(seed * 8 + 3, (batch, M)))
+    y_res, _ = oracle.bfp8_gemv(packed, M, K, x, residual_bits=res)
+    return dict(packed=packed, y=y, y32=y32, y_resadd=y_res)
+
+
 def main():
     for seed, ctx in ATTN_CASES:
         np.savez_compressed(os.path.join(HERE, f"attn_s{seed}_L{ctx}.npz"), seed=seed, ctx=ctx,
@@ -54,6 +65,9 @@ def main():
     for seed, pos in GDN_CASES:
         np.savez_compressed(os.path.join(HERE, f"gdn_s{seed}_p{pos}.npz"), seed=seed,
                             **gdn_case(seed, pos))
+    for seed, M, K, batch in BFP8_CASES:
+        np.savez_compressed(os.path.join(HERE, f"bfp8_s{seed}_{M}x{K}_b{batch}.npz"), seed=seed,
+                            M=M, K=K, batch=batch, **bfp8_case(seed, M, K, batch))
     print("written to", HERE)
 
 
