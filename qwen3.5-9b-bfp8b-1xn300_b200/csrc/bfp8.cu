@@ -14,12 +14,9 @@
 //   - the MMA's k order is permuted so that lane (g, t) owns bytes 4t..4t+3
 //     of face rows g and g + 8: one 32-bit shared load per row, conflict free;
 //     the activations take the same permutation (one 8-byte load per lane);
-//   - byte -> f16: the device layout stores each element as offset binary
-//     u = 128 + (+-m); one byte permute builds the f16 pair with bits
-//     0x64|u (= 1024 + u exactly) for two elements and one f16x2 subtraction
-//     of 1152 leaves +-m — half an integer-pipe op per element;
-//   - the activations enter the f16 MMAs scaled by a power of two per row
-//     (bfp8_xconv_kernel, exact for all but the smallest elements);
+//   - byte -> bf16: the bf16 with high byte sign|0x43 and low byte m is
+//     +-(128 + m) exactly; one bf16x2 subtraction of +-128 leaves +-m.  Two
+//     logic ops and four byte permutes serve four elements;
 //   - each face row's shared exponent scales that face's MMA result (a
 //     fresh f32 accumulator of 16 products) by 2^(e-127) into the running
 //     sum; the decode rule's remaining 2^-6 is applied once per output.  Both
@@ -35,11 +32,9 @@
 // only before it reads activations or writes outputs and scratch.
 
 #include <cuda_bf16.h>
-#include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cstring>
-#include <cstdlib>
 #include <string>
 
 #include "../../include/qbfp8.h"
@@ -62,27 +57,32 @@ struct GemvSmem {
   uint64_t full[NWARP][NSTW];
 };
 
-// Four offset-binary bytes u = 128 + t (t = +-m, the device layout) of one
-// face row -> t as two f16x2 words (elements 0,1 and 2,3): the f16 with bits
-// 0x64 | u is 1024 + u exactly, and one f16x2 subtraction of 1152 leaves t.
+// Four sign/magnitude bytes of one face row -> their signed magnitudes +-m
+// as two bf16x2 words (elements 0,1 and 2,3).  With the high byte s|0x43 and
+// the low byte m, a bf16 is +-(128 + m) exactly; subtracting +-128 leaves +-m.
 __device__ __forceinline__ void mags4(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t v_lo = __byte_perm(w, 0x64646464u, 0x5140);
-  const uint32_t v_hi = __byte_perm(w, 0x64646464u, 0x7362);
-  const __half2 off = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
-  __half2 a;
+  const uint32_t mm = w & 0x7f7f7f7fu;
+  const uint32_t hh = (w & 0x80808080u) | 0x43434343u;
+  const uint32_t v_lo = __byte_perm(mm, hh, 0x5140);
+  const uint32_t v_hi = __byte_perm(mm, hh, 0x7362);
+  const uint32_t s_lo = __byte_perm(0u, hh, 0x5140);
+  const uint32_t s_hi = __byte_perm(0u, hh, 0x7362);
+  __nv_bfloat162 a, b;
   std::memcpy(&a, &v_lo, 4);
-  const __half2 r_lo = __hsub2(a, off);
+  std::memcpy(&b, &s_lo, 4);
+  const __nv_bfloat162 r_lo = __hsub2(a, b);
   std::memcpy(&a, &v_hi, 4);
-  const __half2 r_hi = __hsub2(a, off);
+  std::memcpy(&b, &s_hi, 4);
+  const __nv_bfloat162 r_hi = __hsub2(a, b);
   std::memcpy(&lo, &r_lo, 4);
   std::memcpy(&hi, &r_hi, 4);
 }
 
-// d = A.B (fresh accumulator), f16 operands
-__device__ __forceinline__ void mma_f16_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+// d = A.B (fresh accumulator), bf16 operands
+__device__ __forceinline__ void mma_bf16_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                            uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%10,%10,%10,%10};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
@@ -99,10 +99,59 @@ __device__ __forceinline__ void store_out(const Bfp8GemvArgs& a, int m, int b, f
     *p = f2bf(v);
 }
 
-// The warp's position in its sequence of (unit, first tile) stage loads.
-struct Cursor {
-  int u, c0;
+// A warp's position in its sequence of units (u = first, += W): unit u is
+// k-chunk s = u / Mt of tile-row mt = u % Mt, the ku tiles from k-tile s*ku
+// (contiguous bytes).  s and mt advance by addition (W = Wq * Mt + Wr).
+struct UnitCursor {
+  int u, s, mt, nt;
+  __device__ __forceinline__ void init(const Bfp8GemvArgs& a, int u0) {
+    u = u0;
+    s = u0 / a.Mt;
+    mt = u0 - s * a.Mt;
+    nt = min(a.ku, a.Kt - s * a.ku);
+  }
+  __device__ __forceinline__ void next(const Bfp8GemvArgs& a, int W, int Wq, int Wr) {
+    u += W;
+    s += Wq;
+    mt += Wr;
+    if (mt >= a.Mt) { mt -= a.Mt; ++s; }
+    nt = min(a.ku, a.Kt - s * a.ku);
+  }
 };
+
+// One tile of the device layout times the activation fragments b (per n8
+// column group q: k 4t..4t+3 and 16+4t..16+4t+3 of the tile), accumulated
+// into acc[row block][q][4].
+template <int NT>
+__device__ __forceinline__ void tile_mma(const uint8_t* tile, int g, int lane,
+                                         const uint32_t (&b)[NT][4], float (&acc)[2][NT][4]) {
+  // this lane's 8 shared exponents and 8 words of mantissa bytes
+  const uint2 ex = *reinterpret_cast<const uint2*>(tile + g * 8);
+  const uint4 wa = *reinterpret_cast<const uint4*>(tile + 64 + lane * 16);
+  const uint4 wb = *reinterpret_cast<const uint4*>(tile + 64 + 512 + lane * 16);
+  const uint32_t wr[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+  for (int f = 0; f < 4; ++f) {
+    // 2^(e - 127) per face row; the remaining 2^-6 of the decode rule is
+    // applied once per output (exact: powers of two)
+    const uint32_t ew = f < 2 ? ex.x : ex.y;
+    const float sc0 = __uint_as_float(__byte_perm(ew, 0u, 0x4440 + (f & 1) * 2) << 23);
+    const float sc1 = __uint_as_float(__byte_perm(ew, 0u, 0x4441 + (f & 1) * 2) << 23);
+    uint32_t a0, a1, a2, a3;
+    mags4(wr[2 * f], a0, a2);
+    mags4(wr[2 * f + 1], a1, a3);
+#pragma unroll
+    for (int q = 0; q < NT; ++q) {
+      float d[4];
+      mma_bf16_z(d, a0, a1, a2, a3, b[q][(f & 1) * 2], b[q][(f & 1) * 2 + 1]);
+      float(&c)[4] = acc[f >> 1][q];
+      c[0] = fmaf(sc0, d[0], c[0]);
+      c[1] = fmaf(sc0, d[1], c[1]);
+      c[2] = fmaf(sc1, d[2], c[2]);
+      c[3] = fmaf(sc1, d[3], c[3]);
+    }
+  }
+}
 
 template <int NT>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) bfp8_gemv_kernel(const Bfp8GemvArgs a) {
@@ -110,6 +159,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) bfp8_gemv_kernel(const Bfp8Ge
   GemvSmem& sm = *reinterpret_cast<GemvSmem*>(raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int W = gridDim.x * NWARP, gw = blockIdx.x * NWARP + warp;
+  const int Wq = W / a.Mt, Wr = W - Wq * a.Mt;
   uint64_t* full = sm.full[warp];
   if (lane == 0) {
     for (int i = 0; i < NSTW; ++i) mbar_init(&full[i], 1);
@@ -117,130 +167,97 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) bfp8_gemv_kernel(const Bfp8Ge
   }
   __syncwarp();
 
-  auto unit_tiles = [&](int u) {
-    const int s = u / a.Mt;
-    return min(a.ku, a.Kt - s * a.ku);
-  };
-  // lane 0 loads the next stage of this warp's sequence into slot st
-  auto issue = [&](const Cursor& c, int st) {
-    if (a.diag & 16) {
-      if (lane == 0) mbar_arrive(&full[st]);
-      return;
-    }
+  // copy cursor: the unit and first tile of the next stage to load
+  UnitCursor fu;
+  fu.init(a, gw);
+  int fc0 = 0;
+  auto issue = [&](int st) {  // loads the cursor's stage into slot st and advances
     if (lane == 0) {
-      const int s = c.u / a.Mt, mt = c.u - s * a.Mt;
-      const int n = min(TPS, unit_tiles(c.u) - c.c0);
-      const uint8_t* src = a.w + ((int64_t)mt * a.Kt + s * a.ku + c.c0) * TB;
+      const int n = min(TPS, fu.nt - fc0);
+      const uint8_t* src = a.w + ((int64_t)fu.mt * a.Kt + fu.s * a.ku + fc0) * TB;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive_expect_tx(&full[st], n * TB);
       bulk_g2s(sm.stage[warp][st], src, n * TB, &full[st]);
     }
-  };
-  auto advance = [&](Cursor& c) {
-    c.c0 += TPS;
-    if (c.c0 >= unit_tiles(c.u)) {
-      c.u += W;
-      c.c0 = 0;
+    fc0 += TPS;
+    if (fc0 >= fu.nt) {
+      fu.next(a, W, Wq, Wr);
+      fc0 = 0;
     }
   };
 
   const int g = lane >> 2, t = lane & 3;
-  // B fragments (activations) of tiles kt_first .. kt_first + n - 1
-  auto load_b = [&](uint32_t (&b)[TPS][2][NT][2], int kt_first, int n) {
+  // activation fragments (bf16) of tiles kt_first .. kt_first + n - 1:
+  // per tile and column group, k 4t..4t+3 and 16+4t..16+4t+3
+  auto load_b = [&](uint32_t (&b)[TPS][NT][4], int kt_first, int n) {
 #pragma unroll
     for (int j = 0; j < TPS; ++j)
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int q = 0; q < NT; ++q) {
-          const int col = q * 8 + g;
-          uint2 v = make_uint2(0u, 0u);
-          if (j < n && col < a.batch)
-            v = __ldg(reinterpret_cast<const uint2*>(a.x16 + (int64_t)col * a.K + (kt_first + j) * 32 +
-                                                     h * 16 + 4 * t));
-          b[j][h][q][0] = v.x;
-          b[j][h][q][1] = v.y;
+      for (int q = 0; q < NT; ++q) {
+        const int col = q * 8 + g;
+        uint2 v0 = make_uint2(0u, 0u), v1 = make_uint2(0u, 0u);
+        if (j < n && col < a.batch) {
+          const uint16_t* xp = a.x + (int64_t)col * a.K + (kt_first + j) * 32 + 4 * t;
+          v0 = __ldg(reinterpret_cast<const uint2*>(xp));
+          v1 = __ldg(reinterpret_cast<const uint2*>(xp + 16));
         }
+        b[j][q][0] = v0.x;
+        b[j][q][1] = v0.y;
+        b[j][q][2] = v1.x;
+        b[j][q][3] = v1.y;
+      }
   };
 
   // The next kernel on the stream may start as soon as SMs free up; it only
   // streams its own (read-only) weights until its griddepcontrol.wait.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  Cursor fc{gw, 0};
-  for (int i = 0; i < NSTW && fc.u < a.n_units; ++i) {
-    issue(fc, i);
-    advance(fc);
-  }
+  for (int i = 0; i < NSTW && fu.u < a.n_units; ++i) issue(i);
   // Everything below reads the activations or writes outputs and scratch:
   // wait until the previous kernel on the stream has completed.
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   int st = 0;
   uint32_t ph = 0;
-  for (int u = gw; u < a.n_units; u += W) {
-    const int s = u / a.Mt, mt = u - s * a.Mt;
-    const int kt0 = s * a.ku, nt = unit_tiles(u);
+  bool ok = true;
+  UnitCursor cu;
+  cu.init(a, gw);
+  for (; cu.u < a.n_units; cu.next(a, W, Wq, Wr)) {
+    const int s = cu.s, mt = cu.mt, kt0 = s * a.ku, nt = cu.nt;
     float acc[2][NT][4];
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
       for (int q = 0; q < NT; ++q) acc[i][q][0] = acc[i][q][1] = acc[i][q][2] = acc[i][q][3] = 0.0f;
 
-    // activation fragments of the current stage, and of the next one loaded
-    // while the current one is computed
-    uint32_t bc[TPS][2][NT][2], bn[TPS][2][NT][2];
-    load_b(bc, kt0, min(TPS, nt));
-    for (int c0 = 0; c0 < nt; c0 += TPS) {
-      const int n = min(TPS, nt - c0);
-      if (c0 + TPS < nt) load_b(bn, kt0 + c0 + TPS, min(TPS, nt - c0 - TPS));
-      if (!mbar_wait(&full[st], ph, a.err)) return;
+    // one stage: wait, TPS tiles (or the unit's last n), release by loading
+    // the next stage of the warp's sequence into the same slot
+    auto stage = [&](const uint32_t (&b)[TPS][NT][4], int n) {
+      if (!mbar_wait(&full[st], ph, a.err)) { ok = false; return; }
+      const uint8_t* base = sm.stage[warp][st];
+      if (n == TPS) {
 #pragma unroll
-      for (int j = 0; j < TPS; ++j) {
-        if (j >= n || (a.diag & 1)) break;
-        const uint8_t* tile = sm.stage[warp][st] + j * TB;
-        // device layout (bfp8_transcode_kernel): this lane's 8 exponents and
-        // 8 words of mantissa bytes
-        const uint2 ex = *reinterpret_cast<const uint2*>(tile + g * 8);
-        const uint4 wa = *reinterpret_cast<const uint4*>(tile + 64 + lane * 16);
-        const uint4 wb = *reinterpret_cast<const uint4*>(tile + 64 + 512 + lane * 16);
-        const uint32_t wr[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        for (int j = 0; j < TPS; ++j) tile_mma<NT>(base + j * TB, g, lane, b[j], acc);
+      } else {
 #pragma unroll
-        for (int f = 0; f < 4; ++f) {
-          // 2^(e - 127) per face row; the remaining 2^-6 of the decode rule is
-          // applied once per output (exact: powers of two)
-          const uint32_t ew = f < 2 ? ex.x : ex.y;
-          const float sc0 = __uint_as_float(__byte_perm(ew, 0u, 0x4440 + (f & 1) * 2) << 23);
-          const float sc1 = __uint_as_float(__byte_perm(ew, 0u, 0x4441 + (f & 1) * 2) << 23);
-          uint32_t a0, a1, a2, a3;
-          mags4(wr[2 * f], a0, a2);
-          mags4(wr[2 * f + 1], a1, a3);
-#pragma unroll
-          for (int q = 0; q < NT; ++q) {
-            float d[4];
-            mma_f16_z(d, a0, a1, a2, a3, bc[j][f & 1][q][0], bc[j][f & 1][q][1]);
-            float(&c)[4] = acc[f >> 1][q];
-            c[0] = fmaf(sc0, d[0], c[0]);
-            c[1] = fmaf(sc0, d[1], c[1]);
-            c[2] = fmaf(sc1, d[2], c[2]);
-            c[3] = fmaf(sc1, d[3], c[3]);
-          }
-        }
+        for (int j = 0; j < TPS - 1; ++j)
+          if (j < n) tile_mma<NT>(base + j * TB, g, lane, b[j], acc);
       }
       __syncwarp();
-      if (fc.u < a.n_units) {
-        issue(fc, st);
-        advance(fc);
-      }
+      if (fu.u < a.n_units) issue(st);
       if (++st == NSTW) { st = 0; ph ^= 1u; }
-#pragma unroll
-      for (int j = 0; j < TPS; ++j)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int q = 0; q < NT; ++q) {
-            bc[j][h][q][0] = bn[j][h][q][0];
-            bc[j][h][q][1] = bn[j][h][q][1];
-          }
+    };
+    // activation fragments ping-pong between two register sets: the next
+    // stage's are loaded while the current stage is computed
+    uint32_t bA[TPS][NT][4], bB[TPS][NT][4];
+    load_b(bA, kt0, min(TPS, nt));
+    for (int c0 = 0; c0 < nt; c0 += 2 * TPS) {
+      if (c0 + TPS < nt) load_b(bB, kt0 + c0 + TPS, min(TPS, nt - c0 - TPS));
+      stage(bA, min(TPS, nt - c0));
+      if (!ok) return;
+      if (c0 + TPS >= nt) break;
+      if (c0 + 2 * TPS < nt) load_b(bA, kt0 + c0 + 2 * TPS, min(TPS, nt - c0 - 2 * TPS));
+      stage(bB, min(TPS, nt - c0 - TPS));
+      if (!ok) return;
     }
 
     // ---- unit epilogue: lane (g, t) holds rows g, g+8, g+16, g+24 of the
@@ -250,21 +267,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) bfp8_gemv_kernel(const Bfp8Ge
 #pragma unroll
       for (int q = 0; q < NT; ++q)
 #pragma unroll
-        for (int e = 0; e < 4; ++e)  // 2^-6 of the decode rule, and the activations' scale
-          acc[rb][q][e] *= 0.015625f * a.xscale[min(q * 8 + 2 * t + (e & 1), NMAX - 1)];
-    if (a.diag & 2) continue;
-    if (a.S == 1) {
-#pragma unroll
-      for (int rb = 0; rb < 2; ++rb)
-#pragma unroll
-        for (int q = 0; q < NT; ++q)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int r = rb * 16 + g + (e >> 1) * 8, c = q * 8 + 2 * t + (e & 1);
-            if (c < a.batch) store_out(a, mt * 32 + r, c, acc[rb][q][e]);
-          }
-      continue;
-    }
+        for (int e = 0; e < 4; ++e)  // 2^-6 of the decode rule
+          acc[rb][q][e] *= 0.015625f;
 #pragma unroll
     for (int rb = 0; rb < 2; ++rb)
 #pragma unroll
@@ -272,34 +276,13 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) bfp8_gemv_kernel(const Bfp8Ge
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int r = rb * 16 + g + (e >> 1) * 8, c = q * 8 + 2 * t + (e & 1);
-          if (c < a.batch) a.partial[((int64_t)s * NMAX + c) * a.M + mt * 32 + r] = acc[rb][q][e];
+          if (c >= a.batch) continue;
+          if (a.S == 1)
+            store_out(a, mt * 32 + r, c, acc[rb][q][e]);
+          else
+            a.partial[((int64_t)s * NMAX + c) * a.M + mt * 32 + r] = acc[rb][q][e];
         }
   }
-}
-
-// Activations for the f16 MMAs: row b of x (bf16) scaled by the power of two
-// 2^s that brings max|x| into [2^14, 2^15), then converted to f16 — exact for
-// every element above max|x| * 2^-29 (f16 keeps the 8 significant bits of a
-// bf16 in its normal range); the GEMV multiplies its sums by 2^-s.
-__global__ void __launch_bounds__(256) bfp8_xconv_kernel(const Bfp8GemvArgs a) {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  __shared__ float red[8];
-  const int b = blockIdx.x, tid = threadIdx.x;
-  const uint16_t* x = a.x + (int64_t)b * a.K;
-  float mx = 0.0f;
-  for (int i = tid; i < a.K; i += 256) mx = fmaxf(mx, fabsf(bf2f(x[i])));
-  mx = warp_max(mx);
-  if ((tid & 31) == 0) red[tid >> 5] = mx;
-  __syncthreads();
-  mx = red[0];
-  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
-  int e = 0;
-  if (mx > 0.0f && isfinite(mx)) frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
-  const int sh = (mx > 0.0f && isfinite(mx)) ? 15 - e : 0;
-  uint16_t* y = a.x16w + (int64_t)b * a.K;
-  for (int i = tid; i < a.K; i += 256) y[i] = __half_as_ushort(__float2half_rn(ldexpf(bf2f(x[i]), sh)));
-  if (tid == 0) a.xscalew[b] = ldexpf(1.0f, -sh);
 }
 
 // Split-K merge: one thread per output, the S partials added in k order
@@ -327,9 +310,7 @@ __global__ void __launch_bounds__(256) bfp8_merge_kernel(const Bfp8GemvArgs a) {
 }
 
 // Device layout of a tile (the same 1088 bytes, permuted), built on upload
-// from the GGUF layout and undone on download.  Mantissa bytes become offset
-// binary, 128 + (+-m) (a GGUF "negative zero" byte, which the packer never
-// writes, comes back as +0).  For MMA lane l = 4g + t:
+// from the GGUF layout and undone on download.  For MMA lane l = 4g + t:
 //   bytes [g*8, g*8 + 8): shared exponents of face rows (f, g), (f, g + 8)
 //     for f = 0..3, in that order;
 //   bytes [64 + h*512 + l*16, +16), h = 0, 1: for faces 2h, 2h + 1 the
@@ -364,12 +345,10 @@ __global__ void __launch_bounds__(256) bfp8_transcode_kernel(uint8_t* __restrict
         t[i] = buf[w][o];
       else
         t[o] = buf[w][i];
-    } else if (to_device) {  // sign/magnitude -> offset binary 128 + t
-      const uint32_t b = buf[w][o];
-      t[i] = uint8_t((b & 0x80u) ? 128u - (b & 0x7fu) : 128u + b);
+    } else if (to_device) {
+      t[i] = buf[w][o];
     } else {
-      const int v = int(buf[w][i]) - 128;
-      t[o] = uint8_t(v < 0 ? (0x80 | -v) : v);
+      t[o] = buf[w][i];
     }
   }
 }
@@ -444,15 +423,7 @@ cudaError_t launch_bfp8_gemv(const Bfp8GemvArgs& a, int grid, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cfg.gridDim = dim3(a.batch, 1, 1);
-  cfg.blockDim = dim3(256, 1, 1);
-  cfg.dynamicSmemBytes = 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, bfp8_xconv_kernel, a);
-  if (e != cudaSuccess) return e;
-  cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(GEMV_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = sizeof(GemvSmem);
-  e = a.batch <= 8 ? cudaLaunchKernelEx(&cfg, bfp8_gemv_kernel<1>, a)
+  cudaError_t e = a.batch <= 8 ? cudaLaunchKernelEx(&cfg, bfp8_gemv_kernel<1>, a)
                    : cudaLaunchKernelEx(&cfg, bfp8_gemv_kernel<2>, a);
   if (e != cudaSuccess || a.S == 1) return e;
   cfg.gridDim = dim3((unsigned)(((int64_t)a.batch * a.M + 255) / 256), 1, 1);
@@ -487,8 +458,6 @@ struct qc_bfp8_matrix {
   uint8_t* tiles = nullptr;
   int64_t bytes = 0;
   float* partial = nullptr;  // [S][16][M]
-  uint16_t* x16 = nullptr;   // [16][K] f16 activations of one launch
-  float* xscale = nullptr;   // [16]
   int* err = nullptr;
 };
 
@@ -533,20 +502,16 @@ int run_gemv(qc_bfp8_matrix* m, const uint16_t* x, int32_t batch, uint16_t* y0, 
     a.split = split;
     a.mode = mode;
     a.partial = m->partial;
-    a.x16 = a.x16w = m->x16;
-    a.xscale = a.xscalew = m->xscale;
+    a.ku = m->ku;
+    a.S = m->S;
+    a.n_units = m->Mt * m->S;
     a.err = m->err;
     a.M = m->M;
     a.K = m->K;
     a.Mt = m->Mt;
     a.Kt = m->Kt;
-    a.ku = m->ku;
-    a.S = m->S;
-    a.n_units = m->Mt * m->S;
     a.batch = std::min(cols, batch - b0);
-    if (const char* d = getenv("QC_BFP8_DIAG")) a.diag = atoi(d);
-    cudaError_t e = qc::launch_bfp8_gemv(a, m->nsm * qc::bfp8_gemv_ctas_per_sm(a.batch),
-                                         (cudaStream_t)stream);
+    cudaError_t e = qc::launch_bfp8_gemv(a, m->grid, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "bfp8 gemv launch");
   }
   return QC_OK;
@@ -585,13 +550,14 @@ int qc_bfp8_create(int device, int32_t M, int32_t K, qc_bfp8_matrix** out) {
   m->grid = m->nsm * qc::bfp8_gemv_ctas_per_sm(1);
   // k-chunks per tile-row: the split that minimises the critical path, i.e.
   // (units per warp) x (tiles per unit + the unit epilogue, worth ~1 tile
-  // alone and ~3 with the split-K merge)
+  // alone and ~3 with the split-K merge); chunks of whole 4-tile stages
   const int64_t n_warps = (int64_t)m->grid * qc::bfp8_gemv_warps_per_cta();
   double best = 1e300;
   m->S = 1;
   m->ku = m->Kt;
   for (int32_t S = 1; S <= m->Kt; ++S) {
-    const int32_t ku = (m->Kt + S - 1) / S;
+    int32_t ku = (m->Kt + S - 1) / S;
+    if (m->Kt >= 4) ku = (ku + 3) / 4 * 4;
     if ((m->Kt + ku - 1) / ku != S) continue;
     const int64_t units = (int64_t)m->Mt * S;
     const double cost = (double)((units + n_warps - 1) / n_warps) * (ku + (S > 1 ? 3 : 1));
@@ -605,8 +571,6 @@ int qc_bfp8_create(int device, int32_t M, int32_t K, qc_bfp8_matrix** out) {
   if (e == cudaSuccess) e = cudaMalloc(&m->tiles, (size_t)m->bytes);
   if (e == cudaSuccess && m->S > 1)
     e = cudaMalloc(&m->partial, (size_t)m->S * qc::bfp8_gemv_columns() * M * sizeof(float));
-  if (e == cudaSuccess) e = cudaMalloc(&m->x16, (size_t)qc::bfp8_gemv_columns() * K * 2);
-  if (e == cudaSuccess) e = cudaMalloc(&m->xscale, (size_t)qc::bfp8_gemv_columns() * sizeof(float));
   if (e == cudaSuccess) e = cudaMalloc(&m->err, sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(m->tiles, 0, (size_t)m->bytes);
   if (e == cudaSuccess) e = cudaMemset(m->err, 0, sizeof(int));
@@ -625,8 +589,6 @@ void qc_bfp8_destroy(qc_bfp8_matrix* m) {
   DeviceScope ds(m->device);
   cudaFree(m->tiles);
   cudaFree(m->partial);
-  cudaFree(m->x16);
-  cudaFree(m->xscale);
   cudaFree(m->err);
   delete m;
 }

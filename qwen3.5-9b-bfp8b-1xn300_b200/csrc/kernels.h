@@ -153,14 +153,9 @@ struct Bfp8GemvArgs {
   int64_t ld0, ld1;
   int32_t split;
   int32_t mode;
-  float* partial;   // [S][columns][M] f32
-  const uint16_t* x16;  // [columns][K] f16 activations (scaled), written by the conversion
-  uint16_t* x16w;
-  const float* xscale;  // [columns] 2^-s of each activation row
-  float* xscalew;
+  float* partial;   // [S][columns][M] f32 split-K partial sums
   int* err;
   int32_t M, K, Mt, Kt, ku, S, n_units, batch;
-  int32_t diag;
 };
 cudaError_t bfp8_prepare_device();
 cudaError_t launch_bfp8_gemv(const Bfp8GemvArgs& a, int grid, cudaStream_t s);
