@@ -16,10 +16,11 @@
 //      IEEE double, the same operations as the CPU restatement);
 //   3. radix selection over the 32-bit masses, most significant byte first:
 //      per pass a 256-bin histogram of (mass, count) of the tokens matching
-//      the digits chosen so far — warp-aggregated integer atomics into
-//      per-warp histograms, summed per CTA and across the cluster — then a
-//      scan from the top bin picks the bin where the running mass reaches
-//      the target.  Run once for the nucleus cut (target = top_p * Z) and once
+//      the digits chosen so far — each thread sums runs of its tokens that
+//      share a bin and adds them to its warp's histogram with integer
+//      atomics; the histograms are summed per CTA and across the cluster —
+//      then one warp scans the bins from the top for the one where the
+//      running mass reaches the target.  Run once for the nucleus cut (target = top_p * Z) and once
 //      for the draw (target = u * kept mass);
 //   4. the drawn mass class holds equal-mass tokens in index order; the j-th
 //      is located by per-CTA counts, a prefix over the cluster's ranks and a
@@ -96,32 +97,21 @@ __device__ __forceinline__ double exp_ref(double x) {
 __device__ __forceinline__ uint32_t token_mass(float l, float max_l, float inv_t) {
   if (isnan(l)) return 0u;
   const float x = __fmul_rn(__fsub_rn(l, max_l), inv_t);
+  // exp(-22.2) * 2^31 < 0.49: such tokens round to mass 0 (as they do in
+  // the CPU restatement, which evaluates the exponential)
+  if (x < -22.2f) return 0u;
   return (uint32_t)rint(exp_ref((double)x) * 2147483648.0);
-}
-
-// Adds (q, 1) to bin `bin` of this warp's histogram, one atomic per group of
-// lanes that share a bin (active lanes given by `active`).
-__device__ __forceinline__ void hist_add(SampleSmem& sm, int warp, bool active, uint32_t bin,
-                                         uint32_t q) {
-  const unsigned act = __ballot_sync(FULL_MASK, active);
-  if (!active) return;
-  const unsigned peers = __match_any_sync(act, bin);
-  const uint32_t lo = __reduce_add_sync(peers, q & 0xffffu);
-  const uint32_t hi = __reduce_add_sync(peers, q >> 16);
-  const uint32_t n = __popc(peers);
-  if ((threadIdx.x & 31) == __ffs(peers) - 1) {
-    atomicAdd(&sm.wmass[warp][bin], (unsigned long long)lo + ((unsigned long long)hi << 16));
-    atomicAdd(&sm.wcnt[warp][bin], n);
-  }
 }
 
 // Selects the mass class at which the running mass (tokens in decreasing
 // mass) first reaches `target`, restricted to nonempty classes.  Returns the
 // class's mass value, the mass of all heavier tokens, and its token count.
+// Tokens lighter than `lo` are left out: the caller knows the answer is at
+// or above it (the draw lies inside the nucleus).
 __device__ void radix_select(SampleSmem& sm, cg::cluster_group& cluster, int n_local,
-                             unsigned long long target, uint32_t& value,
+                             uint32_t lo, unsigned long long target, uint32_t& value,
                              unsigned long long& above, uint32_t& count) {
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint32_t prefix = 0, mask = 0;
   unsigned long long run = 0;
   for (int b = 3; b >= 0; --b) {
@@ -130,16 +120,37 @@ __device__ void radix_select(SampleSmem& sm, cg::cluster_group& cluster, int n_l
       (&sm.wcnt[0][0])[i] = 0u;
     }
     __syncthreads();
-    for (int i0 = 0; i0 < n_local; i0 += ST) {
-      const int i = i0 + tid;
-      const uint32_t q = i < n_local ? sm.q[i] : 0u;
-      const bool match = i < n_local && (q & mask) == prefix;
-      hist_add(sm, warp, match, (q >> (8 * b)) & 255u, q);
+    // each thread sums runs of its own tokens that share a bin (most share
+    // the lowest one) and flushes a run to its warp's histogram when the bin
+    // changes: integer sums, so the order of the atomics does not matter
+    int cur = -1;
+    unsigned long long run_m = 0;
+    uint32_t run_c = 0;
+    for (int i = tid; i < n_local; i += ST) {
+      const uint32_t q = sm.q[i];
+      if (q < lo || (q & mask) != prefix) continue;
+      const int bin = (int)((q >> (8 * b)) & 255u);
+      if (bin != cur) {
+        if (cur >= 0) {
+          atomicAdd(&sm.wmass[warp][cur], run_m);
+          atomicAdd(&sm.wcnt[warp][cur], run_c);
+        }
+        cur = bin;
+        run_m = 0;
+        run_c = 0;
+      }
+      run_m += q;
+      ++run_c;
+    }
+    if (cur >= 0) {
+      atomicAdd(&sm.wmass[warp][cur], run_m);
+      atomicAdd(&sm.wcnt[warp][cur], run_c);
     }
     __syncthreads();
     if (tid < 256) {
       unsigned long long m = 0;
       uint32_t c = 0;
+#pragma unroll
       for (int w = 0; w < SW; ++w) {
         m += sm.wmass[w][tid];
         c += sm.wcnt[w][tid];
@@ -151,6 +162,7 @@ __device__ void radix_select(SampleSmem& sm, cg::cluster_group& cluster, int n_l
     if (tid < 256) {
       unsigned long long m = 0;
       uint32_t c = 0;
+#pragma unroll
       for (int r = 0; r < SC; ++r) {
         m += *cluster.map_shared_rank(&sm.mass[tid], r);
         c += *cluster.map_shared_rank(&sm.cnt[tid], r);
@@ -159,25 +171,46 @@ __device__ void radix_select(SampleSmem& sm, cg::cluster_group& cluster, int n_l
       sm.gcnt[tid] = c;
     }
     cluster.sync();  // all peers have read this pass's histograms
-    if (tid == 0) {
-      int sel = -1;
-      unsigned long long r = run;
-      for (int bin = 255; bin >= 0; --bin) {
-        if (sm.gcnt[bin] == 0) continue;
-        if (r + sm.gmass[bin] >= target) {
-          sel = bin;
-          break;
-        }
-        r += sm.gmass[bin];
+    if (warp == 0) {
+      // bins in decreasing order, 8 per lane: lane l owns bins 255-8l .. 248-8l
+      unsigned long long bm[8], own = 0;
+      uint32_t bc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        bm[e] = sm.gmass[255 - 8 * lane - e];
+        bc[e] = sm.gcnt[255 - 8 * lane - e];
+        own += bm[e];
       }
-      if (sel < 0) {  // unreachable (targets never exceed the total): lightest class
-        r = run;
+      unsigned long long before = own;
+#pragma unroll
+      for (int m = 1; m < 32; m <<= 1) {
+        const unsigned long long o = __shfl_up_sync(FULL_MASK, before, m);
+        if (lane >= m) before += o;
+      }
+      before -= own;  // mass of the heavier bins, owned by lower lanes
+      int found = -1;
+      unsigned long long r = run + before;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (found >= 0) continue;
+        if (bc[e] != 0 && r + bm[e] >= target) found = e;
+        else r += bm[e];
+      }
+      const unsigned hit = __ballot_sync(FULL_MASK, found >= 0);
+      if (hit) {
+        if (lane == __ffs(hit) - 1) {
+          sm.sel_bin = 255 - 8 * lane - found;
+          sm.sel_above = r;
+        }
+      } else if (lane == 0) {  // unreachable (targets never exceed the total): lightest class
+        int sel = -1;
+        unsigned long long rr = run;
         for (int bin = 0; bin < 256; ++bin)
           if (sm.gcnt[bin]) { sel = bin; break; }
-        for (int bin = 255; bin > sel; --bin) r += sm.gmass[bin];
+        for (int bin = 255; bin > sel; --bin) rr += sm.gmass[bin];
+        sm.sel_bin = sel;
+        sm.sel_above = rr;
       }
-      sm.sel_bin = sel;
-      sm.sel_above = r;
     }
     __syncthreads();
     prefix |= (uint32_t)sm.sel_bin << (8 * b);
@@ -269,7 +302,7 @@ __global__ void __launch_bounds__(ST, 1) sample_kernel(const SampleArgs a) {
   const unsigned long long target = (unsigned long long)((double)a.top_p * (double)z);
   uint32_t theta, cnt_theta;
   unsigned long long above;
-  radix_select(sm, cluster, n_local, target, theta, above, cnt_theta);
+  radix_select(sm, cluster, n_local, 0u, target, theta, above, cnt_theta);
   unsigned long long k = theta ? (target > above ? (target - above + theta - 1) / theta : 0) : 1;
   if (k < 1) k = 1;
   if (k > cnt_theta) k = cnt_theta;
@@ -277,7 +310,7 @@ __global__ void __launch_bounds__(ST, 1) sample_kernel(const SampleArgs a) {
   const unsigned long long rdraw = (unsigned long long)(a.uniform[row] * (double)kept);
   uint32_t kappa, cnt_kappa;
   unsigned long long above2;
-  radix_select(sm, cluster, n_local, rdraw, kappa, above2, cnt_kappa);
+  radix_select(sm, cluster, n_local, theta, rdraw, kappa, above2, cnt_kappa);
   unsigned long long j = (rdraw > above2 && kappa) ? (rdraw - above2 + kappa - 1) / kappa : 1;
   if (j < 1) j = 1;
 
@@ -288,14 +321,22 @@ __global__ void __launch_bounds__(ST, 1) sample_kernel(const SampleArgs a) {
   for (int i = s0; i < s1; ++i) c += sm.q[i] == kappa;
   sm.scan[tid] = c;
   __syncthreads();
-  if (tid == 0) {  // exclusive scan over the threads, then this CTA's total
-    int run = 0;
-    for (int t = 0; t < ST; ++t) {
-      const int x = sm.scan[t];
-      sm.scan[t] = run;
-      run += x;
+  {  // exclusive scan over the threads (warp shuffles, then the warp totals)
+    int incl = c;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+      const int o = __shfl_up_sync(FULL_MASK, incl, m);
+      if (lane >= m) incl += o;
     }
-    for (int r = 0; r < SC; ++r) *cluster.map_shared_rank(&sm.rank_cnt[rank], r) = run;
+    if (lane == 31) sm.red_i[warp] = incl;
+    __syncthreads();
+    int wbase = 0;
+    for (int w = 0; w < warp; ++w) wbase += sm.red_i[w];
+    sm.scan[tid] = wbase + incl - c;
+    if (tid == ST - 1) {
+      const int total = wbase + incl;
+      for (int r = 0; r < SC; ++r) *cluster.map_shared_rank(&sm.rank_cnt[rank], r) = total;
+    }
   }
   cluster.sync();
   long long before = 0;
