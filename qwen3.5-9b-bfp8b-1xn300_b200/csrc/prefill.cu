@@ -80,17 +80,33 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArg
 
   // ---- phase A: the chunk's conv outputs of the head's q and k channels and
   // of this CTA's v channels (computed once per chunk by the conv kernel)
-  constexpr int NCH = 2 * HK + GRB;
-#pragma unroll 4
-  for (int idx = tid; idx < T * NCH; idx += 256) {
-    const int t = idx / NCH, ch = idx % NCH;
-    const int c = (ch < HK) ? kh * HK + ch
-                : (ch < 2 * HK) ? 2048 + kh * HK + (ch - HK)
-                                : 4096 + vh * HK + r * GRB + (ch - 2 * HK);
-    const float y = a.conv_out[(int64_t)t * CONV + c];
-    if (ch < HK) sm.q[t][ch] = y;
-    else if (ch < 2 * HK) sm.k[t][ch - HK] = y;
-    else sm.v[t][ch - 2 * HK] = y;
+  // per token: 32 float4 of q, 32 of k, 4 of this CTA's v; all of a thread's
+  // loads are issued before any is stored
+  constexpr int NV4 = 2 * HK / 4 + GRB / 4;  // 68
+  constexpr int NLD = (TMAX * NV4 + 255) / 256;
+  {
+    float4 buf[NLD];
+#pragma unroll
+    for (int u = 0; u < NLD; ++u) {
+      const int idx = tid + 256 * u;
+      buf[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (idx < T * NV4) {
+        const int t = idx / NV4, e = idx % NV4;
+        const int c = (e < 32) ? kh * HK + 4 * e
+                    : (e < 64) ? 2048 + kh * HK + 4 * (e - 32)
+                               : 4096 + vh * HK + r * GRB + 4 * (e - 64);
+        buf[u] = *reinterpret_cast<const float4*>(a.conv_out + (int64_t)t * CONV + c);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < NLD; ++u) {
+      const int idx = tid + 256 * u;
+      if (idx < T * NV4) {
+        const int t = idx / NV4, e = idx % NV4;
+        float* dst = (e < 32) ? &sm.q[t][4 * e] : (e < 64) ? &sm.k[t][4 * (e - 32)] : &sm.v[t][4 * (e - 64)];
+        *reinterpret_cast<float4*>(dst) = buf[u];
+      }
+    }
   }
   if (tid < T) {  // decay and beta (src/engine.cpp:3277-3281)
     const uint16_t* x = a.proj + (int64_t)tid * 12352;
