@@ -62,6 +62,7 @@ struct GdnPrefillSmem {
   float o[TMAX][GRB];
   float decay[TMAX];
   float beta[TMAX];
+  float kq[TMAX];                // k_t . q_t of the normalised vectors
   float ssq[GR][TMAX];          // per-token partial sums of squares, slot per CTA
 };
 
@@ -127,6 +128,8 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArg
     k4.x *= ks; k4.y *= ks; k4.z *= ks; k4.w *= ks;
     reinterpret_cast<float4*>(sm.q[t])[lane] = q4;
     reinterpret_cast<float4*>(sm.k[t])[lane] = k4;
+    const float kq = warp_sum(q4.x * k4.x + q4.y * k4.y + q4.z * k4.z + q4.w * k4.w);
+    if (lane == 0) sm.kq[t] = kq;
   }
   __syncthreads();
 
@@ -136,42 +139,43 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArg
   float4 S[GRPW];
 #pragma unroll
   for (int i = 0; i < GRPW; ++i) S[i] = reinterpret_cast<const float4*>(st)[(row0 + i) * 32 + lane];
+  // Per token both dot products read the state before the token: with
+  // sk = decay (S.k), d = beta (v - sk) and S' = decay S + d k^T, the
+  // output is S'.q = decay (S.q) + d (k.q) — one reduction tree per token
+  // instead of two in sequence.
   for (int t = 0; t < T; ++t) {
     const float4 k4 = reinterpret_cast<const float4*>(sm.k[t])[lane];
     const float4 q4 = reinterpret_cast<const float4*>(sm.q[t])[lane];
-    const float dec = sm.decay[t], bt = sm.beta[t];
-    float sk[GRPW];
+    const float dec = sm.decay[t], bt = sm.beta[t], kq = sm.kq[t];
+    float sk[GRPW], sq[GRPW];
 #pragma unroll
     for (int i = 0; i < GRPW; ++i) {
-      S[i].x *= dec; S[i].y *= dec; S[i].z *= dec; S[i].w *= dec;
       float d = S[i].x * k4.x;
       d = fmaf(S[i].y, k4.y, d);
       d = fmaf(S[i].z, k4.z, d);
-      d = fmaf(S[i].w, k4.w, d);
-      sk[i] = d;
+      sk[i] = fmaf(S[i].w, k4.w, d);
+      float e = S[i].x * q4.x;
+      e = fmaf(S[i].y, q4.y, e);
+      e = fmaf(S[i].z, q4.z, e);
+      sq[i] = fmaf(S[i].w, q4.w, e);
     }
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1)
 #pragma unroll
-      for (int i = 0; i < GRPW; ++i) sk[i] += __shfl_xor_sync(FULL_MASK, sk[i], m);
+      for (int i = 0; i < GRPW; ++i) {
+        sk[i] += __shfl_xor_sync(FULL_MASK, sk[i], m);
+        sq[i] += __shfl_xor_sync(FULL_MASK, sq[i], m);
+      }
     float o[GRPW];
 #pragma unroll
     for (int i = 0; i < GRPW; ++i) {
-      const float dd = bt * (sm.v[t][row0 + i] - sk[i]);
-      S[i].x = fmaf(k4.x, dd, S[i].x);
-      S[i].y = fmaf(k4.y, dd, S[i].y);
-      S[i].z = fmaf(k4.z, dd, S[i].z);
-      S[i].w = fmaf(k4.w, dd, S[i].w);
-      float d = S[i].x * q4.x;
-      d = fmaf(S[i].y, q4.y, d);
-      d = fmaf(S[i].z, q4.z, d);
-      d = fmaf(S[i].w, q4.w, d);
-      o[i] = d;
+      const float dd = bt * (sm.v[t][row0 + i] - dec * sk[i]);
+      S[i].x = fmaf(k4.x, dd, S[i].x * dec);
+      S[i].y = fmaf(k4.y, dd, S[i].y * dec);
+      S[i].z = fmaf(k4.z, dd, S[i].z * dec);
+      S[i].w = fmaf(k4.w, dd, S[i].w * dec);
+      o[i] = fmaf(dd, kq, dec * sq[i]);
     }
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1)
-#pragma unroll
-      for (int i = 0; i < GRPW; ++i) o[i] += __shfl_xor_sync(FULL_MASK, o[i], m);
     if (lane < GRPW) {
       float ov = o[0];
 #pragma unroll
