@@ -596,6 +596,7 @@ void qc_bfp8_destroy(qc_bfp8_matrix* m) {
 void* qc_bfp8_tiles(const qc_bfp8_matrix* m) { return m ? m->tiles : nullptr; }
 
 int qc_bfp8_upload(qc_bfp8_matrix* m, const void* packed_host, qc_stream stream) {
+  qc::TraceRange trace_("qc_bfp8_upload");
   if (!m || !packed_host) return fail(QC_ERR_ARG, "qc_bfp8_upload: bad arguments");
   DeviceScope ds(m->device);
   cudaError_t e = cudaMemcpyAsync(m->tiles, packed_host, (size_t)m->bytes, cudaMemcpyHostToDevice,
@@ -619,6 +620,7 @@ int qc_bfp8_download(qc_bfp8_matrix* m, void* packed_host, qc_stream stream) {
 }
 
 int qc_bfp8_pack_bf16(qc_bfp8_matrix* m, const uint16_t* w_dev, qc_stream stream) {
+  qc::TraceRange trace_("qc_bfp8_pack_bf16");
   if (!m || !w_dev) return fail(QC_ERR_ARG, "qc_bfp8_pack_bf16: bad arguments");
   if (reinterpret_cast<uintptr_t>(w_dev) & 15u)
     return fail(QC_ERR_ARG, "qc_bfp8_pack_bf16: w_dev must be 16-byte aligned");
@@ -631,18 +633,21 @@ int qc_bfp8_pack_bf16(qc_bfp8_matrix* m, const uint16_t* w_dev, qc_stream stream
 
 int qc_bfp8_gemv(qc_bfp8_matrix* m, const uint16_t* x_dev, int32_t batch, uint16_t* y_dev,
                  qc_stream stream) {
+  qc::TraceRange trace_("qc_bfp8_gemv");
   if (!m) return fail(QC_ERR_ARG, "qc_bfp8_gemv: matrix is NULL");
   return run_gemv(m, x_dev, batch, y_dev, m->M, nullptr, 0, m->M, 0, stream);
 }
 
 int qc_bfp8_gemv_resadd(qc_bfp8_matrix* m, const uint16_t* x_dev, int32_t batch,
                         uint16_t* residual_dev, qc_stream stream) {
+  qc::TraceRange trace_("qc_bfp8_gemv_resadd");
   if (!m) return fail(QC_ERR_ARG, "qc_bfp8_gemv_resadd: matrix is NULL");
   return run_gemv(m, x_dev, batch, residual_dev, m->M, nullptr, 0, m->M, 1, stream);
 }
 
 int qc_bfp8_gemv_split(qc_bfp8_matrix* m, const uint16_t* x_dev, int32_t batch, int32_t split_m,
                        uint16_t* y0_dev, uint16_t* y1_dev, qc_stream stream) {
+  qc::TraceRange trace_("qc_bfp8_gemv_split");
   if (!m) return fail(QC_ERR_ARG, "qc_bfp8_gemv_split: matrix is NULL");
   if (split_m <= 0 || split_m >= m->M)
     return fail(QC_ERR_ARG, "qc_bfp8_gemv_split: split_m must be in (0, M)");

@@ -6,7 +6,19 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 namespace qc {
+
+// NVTX range around one C-ABI call (named in a profiler's timeline; a no-op
+// when no tool is attached).
+struct TraceRange {
+  explicit TraceRange(const char* name) { nvtxRangePushA(name); }
+  ~TraceRange() { nvtxRangePop(); }
+  TraceRange(const TraceRange&) = delete;
+  TraceRange& operator=(const TraceRange&) = delete;
+};
+
 
 // Gated-DeltaNet decode step (gdn_decode.cu).
 struct GdnArgs {

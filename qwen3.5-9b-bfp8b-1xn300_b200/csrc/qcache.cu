@@ -650,6 +650,7 @@ int qc_gdn_state_read(qc_ctx* c, int32_t s, int layer, float* state, uint16_t* c
 
 int qc_decode_begin(qc_ctx* c, const int32_t* seq_ids, int32_t n, const int32_t* tokens,
                     qc_stream stream) {
+  qc::TraceRange trace_("qc_decode_begin");
   if (!c || !seq_ids) return QC_ERR_ARG;
   if (c->in_step) return fail(c, QC_ERR_ARG, "decode step already open");
   if (c->in_prefill) return fail(c, QC_ERR_ARG, "prefill chunk open");
@@ -725,6 +726,7 @@ int qc_decode_begin(qc_ctx* c, const int32_t* seq_ids, int32_t n, const int32_t*
 }
 
 int qc_attn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc_stream stream) {
+  qc::TraceRange trace_("qc_attn_decode");
   if (!c || !proj || !out) return QC_ERR_ARG;
   if (!c->in_step) return fail(c, QC_ERR_ARG, "no open decode step");
   if (layer < 0 || layer >= c->cfg.n_attn_layers) return fail(c, QC_ERR_ARG, "attn layer %d", layer);
@@ -768,6 +770,7 @@ int qc_attn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc
 }
 
 int qc_gdn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc_stream stream) {
+  qc::TraceRange trace_("qc_gdn_decode");
   if (!c || !proj || !out) return QC_ERR_ARG;
   if (!c->in_step) return fail(c, QC_ERR_ARG, "no open decode step");
   if (layer < 0 || layer >= c->cfg.n_gdn_layers) return fail(c, QC_ERR_ARG, "gdn layer %d", layer);
@@ -861,6 +864,7 @@ int qc_prefill_begin(qc_ctx* c, int32_t s, int32_t n, const int32_t* tokens, qc_
 }
 
 int qc_attn_prefill(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc_stream stream) {
+  qc::TraceRange trace_("qc_attn_prefill");
   if (!c || !proj || !out) return QC_ERR_ARG;
   if (!c->in_prefill) return fail(c, QC_ERR_ARG, "no open prefill chunk");
   if (layer < 0 || layer >= c->cfg.n_attn_layers) return fail(c, QC_ERR_ARG, "attn layer %d", layer);
@@ -891,6 +895,7 @@ int qc_attn_prefill(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, q
 }
 
 int qc_gdn_prefill(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc_stream stream) {
+  qc::TraceRange trace_("qc_gdn_prefill");
   if (!c || !proj || !out) return QC_ERR_ARG;
   if (!c->in_prefill) return fail(c, QC_ERR_ARG, "no open prefill chunk");
   if (layer < 0 || layer >= c->cfg.n_gdn_layers) return fail(c, QC_ERR_ARG, "gdn layer %d", layer);
@@ -926,6 +931,7 @@ int qc_prefill_end(qc_ctx* c) {
 
 int qc_seq_match_prefix(qc_ctx* c, int32_t s, const int32_t* tokens, int32_t n,
                         int32_t* prefix_len, qc_stream stream) {
+  qc::TraceRange trace_("qc_seq_match_prefix");
   if (!c || (!tokens && n > 0) || !prefix_len) return QC_ERR_ARG;
   if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
   const Seq& q = c->seqs[s];
@@ -961,6 +967,7 @@ int qc_prefix_page_hashes(const int32_t* tokens, int32_t n, uint64_t* hashes) {
 
 int qc_prefix_insert(qc_ctx* c, int32_t s, const int32_t* tokens, int32_t n, int32_t* entry,
                      qc_stream stream) {
+  qc::TraceRange trace_("qc_prefix_insert");
   if (!c || !tokens || !entry || n <= 0) return QC_ERR_ARG;
   if (!valid_seq(c, s)) return fail(c, QC_ERR_ARG, "sequence %d is not live", s);
   if (c->in_step || c->in_prefill) return fail(c, QC_ERR_ARG, "insert inside an open step");
@@ -1019,6 +1026,7 @@ int qc_prefix_insert(qc_ctx* c, int32_t s, const int32_t* tokens, int32_t n, int
 
 int qc_prefix_lookup(qc_ctx* c, const int32_t* tokens, int32_t n, int32_t* matched,
                      int32_t* entry) {
+  qc::TraceRange trace_("qc_prefix_lookup");
   if (!c || (!tokens && n > 0) || !matched || !entry) return QC_ERR_ARG;
   *matched = 0;
   *entry = -1;
@@ -1049,6 +1057,7 @@ int qc_prefix_lookup(qc_ctx* c, const int32_t* tokens, int32_t n, int32_t* match
 
 int qc_prefix_restore(qc_ctx* c, const int32_t* entries, const int32_t* seqs, int32_t n,
                       qc_stream stream) {
+  qc::TraceRange trace_("qc_prefix_restore");
   if (!c || !entries || !seqs || n < 0) return QC_ERR_ARG;
   if (c->in_step || c->in_prefill) return fail(c, QC_ERR_ARG, "restore inside an open step");
   for (int32_t i = 0; i < n; ++i) {
@@ -1161,6 +1170,7 @@ int qc_attn_partial_range(qc_ctx* c, int32_t page_begin, int32_t page_end, int32
 
 int qc_attn_partial(qc_ctx* c, int layer, const uint16_t* proj, float* partial,
                     qc_stream stream) {
+  qc::TraceRange trace_("qc_attn_partial");
   if (!c || !proj || !partial) return QC_ERR_ARG;
   if (!c->in_step) return fail(c, QC_ERR_ARG, "no open decode step");
   if (c->b_seq.size() != 1) return fail(c, QC_ERR_ARG, "split-K needs a batch of 1");
@@ -1207,6 +1217,7 @@ int qc_attn_partial(qc_ctx* c, int layer, const uint16_t* proj, float* partial,
 
 int qc_attn_combine(qc_ctx* c, const float* partials, int32_t n_parts, const uint16_t* proj,
                     uint16_t* out, qc_stream stream) {
+  qc::TraceRange trace_("qc_attn_combine");
   if (!c || !partials || !proj || !out || n_parts <= 0) return QC_ERR_ARG;
   QC_NEED_DEVICE(c);
   QC_CUDA(c, qc::launch_attn_merge_records(partials, n_parts, proj, out, (cudaStream_t)stream));

@@ -392,6 +392,7 @@ cudaError_t launch_sample(const SampleArgs& a, cudaStream_t s) {
 extern "C" int qc_sample(const uint16_t* logits_dev, int64_t ld, int32_t vocab, int32_t batch,
                          float temperature, float top_p, const double* uniform_dev,
                          int32_t* tokens_dev, qc_stream stream) {
+  qc::TraceRange trace_("qc_sample");
   if (!logits_dev || !tokens_dev || batch < 1 || vocab < 1 || vocab > QC_SAMPLE_MAX_VOCAB ||
       ld < vocab || !(top_p > 0.0f && top_p <= 1.0f) ||
       (temperature > 1e-7f && !uniform_dev)) {
