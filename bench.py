@@ -424,6 +424,14 @@ def run_long_split(args, rank, world, dist, n_layers, ctx):
     cuts = [r * pages0 // world for r in range(world)] + [None]
     recs = torch.zeros(n_layers, 16, 258, device="cuda")
     gathered = torch.zeros(n_layers, world, 16, 258, device="cuda")
+    p2p = args.collective == "p2p"
+    if p2p:  # mailboxes in peer memory: handles exchanged once over the process group
+        handle = q.p2p_create(world, rank)
+        handles = [None] * world
+        dist.all_gather_object(handles, handle)
+        for r in range(world):
+            if r != rank:
+                q.p2p_open(r, handles[r])
 
     def begin():
         q.decode_begin(stack.seqs, stream=stream)
@@ -433,6 +441,10 @@ def run_long_split(args, rank, world, dist, n_layers, ctx):
 
     def layers(st):
         for l in range(n_layers):
+            if p2p:
+                q.attn_partial_p2p(l, stack.proj[l].data_ptr(), st)
+                q.attn_combine_p2p(l, stack.proj[l].data_ptr(), stack.out[l].data_ptr(), st)
+                continue
             q.attn_partial(l, stack.proj[l].data_ptr(), recs[l].data_ptr(), st)
             dist.all_gather_into_tensor(gathered[l], recs[l])
             q.attn_combine(gathered[l].data_ptr(), world, stack.proj[l].data_ptr(),
@@ -485,8 +497,12 @@ def run_long_split(args, rank, world, dist, n_layers, ctx):
     return dict(ms=ms, e2e_ms=None, attn_ms=ms, gdn_ms=0.0,
                 attn_layer_bytes=attn_b / args.steps / world, gdn_layer_bytes=0.0, n_local=1,
                 h2d=0, d2h=0, clocks=clk, l2="inputs larger than L2 on every step",
-                collective="NCCL all-gather of the (m, l, o) records, one per layer, "
-                           "captured with the kernels in a CUDA graph")
+                collective=("records stored into every rank's mailbox in peer memory over "
+                            "NVLink by the record kernel, arrival counters bumped at system "
+                            "scope, bounded device-side wait in the merge; captured in a CUDA "
+                            "graph" if p2p else
+                            "NCCL all-gather of the (m, l, o) records, one per layer, "
+                            "captured with the kernels in a CUDA graph"))
 
 
 def run_prefix(args):
@@ -866,6 +882,8 @@ def main():
     ap.add_argument("--seqs", type=int, default=None,
                     help="total sequences (default: the configuration's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--collective", choices=["p2p", "nccl"], default="p2p",
+                    help="config long over several GPUs: how the split-K records travel")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

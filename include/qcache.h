@@ -64,6 +64,7 @@ extern "C" {
  * would touch the GPU returns QC_ERR_NODEVICE.  It exists to test the host
  * logic on machines without a GPU; it computes nothing. */
 #define QC_DEVICE_NONE   (-1)
+#define QC_P2P_MAX_RANKS 8
 
 typedef struct qc_ctx qc_ctx;
 typedef void* qc_stream;   /* cudaStream_t */
@@ -238,6 +239,31 @@ int qc_attn_partial(qc_ctx* ctx, int attn_layer, const uint16_t* proj_dev, float
                     qc_stream stream);
 int qc_attn_combine(qc_ctx* ctx, const float* partials_dev, int32_t n_parts,
                     const uint16_t* proj_dev, uint16_t* out_dev, qc_stream stream);
+
+/* The same split with the records exchanged through peer memory over NVLink
+ * instead of a collective library (one process per GPU, all on one node):
+ *   qc_p2p_create: allocates this rank's mailbox (records of every layer and
+ *     rank, double-buffered by step, plus arrival counters) and writes its
+ *     CUDA IPC handle (QC_P2P_HANDLE_BYTES) to handle_out; the caller ships
+ *     the handles between its processes (any transport);
+ *   qc_p2p_open: maps peer rank `peer`'s mailbox from its handle (every rank
+ *     other than this one, once);
+ *   qc_attn_partial_p2p: like qc_attn_partial, but the kernel that merges the
+ *     range's record stores it into every rank's mailbox (peer stores over
+ *     NVLink) and then bumps every rank's counter for (layer, this rank);
+ *   qc_attn_combine_p2p: waits on the device until all ranks' records of the
+ *     step have arrived (bounded: after 1 s the error word reports
+ *     QC_ERR_TIMEOUT, see qc_check_device, and the output is not written),
+ *     then merges them as qc_attn_combine does.
+ * Every rank must run the same steps and layers (qc_attn_partial_range opens
+ * a step).  Destroy the contexts only after all ranks have finished their
+ * last step. */
+#define QC_P2P_HANDLE_BYTES 64
+int qc_p2p_create(qc_ctx* ctx, int32_t world, int32_t rank, void* handle_out);
+int qc_p2p_open(qc_ctx* ctx, int32_t peer, const void* handle);
+int qc_attn_partial_p2p(qc_ctx* ctx, int attn_layer, const uint16_t* proj_dev, qc_stream stream);
+int qc_attn_combine_p2p(qc_ctx* ctx, int attn_layer, const uint16_t* proj_dev, uint16_t* out_dev,
+                        qc_stream stream);
 
 /* ------------------------------------------- decode without device allocation */
 

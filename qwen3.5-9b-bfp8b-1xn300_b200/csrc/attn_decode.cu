@@ -486,6 +486,27 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (cur_b >= 0) flush();
 }
 
+// Writes head h's record (m, l, o[thread]) into slot [step & 1][layer][rank]
+// of every rank's mailbox over NVLink (plain peer stores), then — once the
+// CTA's stores are visible system-wide — adds 1 to counter [layer][rank] of
+// every rank.  Every CTA of the record kernel does this for its head, so a
+// rank's record for a step is complete when the counter reaches 16 per step.
+__device__ __forceinline__ void publish_record(const CombineArgs& c, int h, float m, float l,
+                                               float o) {
+  const int t = threadIdx.x;
+  const int par = (int)((c.done[c.layer] + 1u) & 1u);  // this step's mailbox half
+  const int64_t off =
+      ((((int64_t)par * c.n_layers + c.layer) * c.world + c.rank) * 16 + h) * (HD + 2);
+  for (int r = 0; r < c.world; ++r) {
+    float* rec = c.mbox_rec[r] + off;
+    if (t == 0) { rec[0] = m; rec[1] = l; }
+    rec[2 + t] = o;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (t < c.world) atomicAdd_system(c.mbox_cnt[t] + c.layer * c.world + c.rank, 1u);
+}
+
 // One CTA per (sequence, kv-head pair, head of the group); the slots of the
 // CTAs that covered the pair (at most one per SM, plus one) are weighed in
 // parallel first, so the per-dimension merge below is a chain of independent
@@ -499,6 +520,10 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const CombineArgs c) 
   const int u0 = c.seg[b] + kvh * np;
   const int per = c.split[1];
   if (np == 0) {  // empty page range (split over devices): an empty record
+    if (c.world > 0) {
+      publish_record(c, kvh * 4 + hh, -INFINITY, 0.0f, 0.0f);
+      return;
+    }
     float* rec = c.record + (kvh * 4 + hh) * (HD + 2);
     if (t == 0) { rec[0] = -INFINITY; rec[1] = 0.0f; }
     rec[2 + t] = 0.0f;
@@ -535,6 +560,10 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const CombineArgs c) 
 #pragma unroll 8
   for (int k = 0; k < ns; ++k) O = fmaf(s_w[k], po[(int64_t)k * 4 * HD], O);
   const int h = kvh * 4 + hh;
+  if (c.world > 0) {  // partial of a split over devices, sent to every rank
+    publish_record(c, h, M, L, O);
+    return;
+  }
   if (c.record) {  // partial of a split over devices: keep it unnormalised
     float* rec = c.record + h * (HD + 2);
     if (t == 0) { rec[0] = M; rec[1] = L; }
@@ -563,7 +592,63 @@ __global__ void __launch_bounds__(256) attn_merge_records_kernel(const float* re
   out[h * HD + t] = f2bf((O / L) * sigmoid_exact(gt));
 }
 
+// The cross-device merge from this rank's mailbox.  The step is done[layer] + 1
+// (this rank's merges so far, counted on the device, so captured and replayed
+// calls number their steps the same way as direct ones).  Thread 0 waits until
+// the counters of all ranks for this layer reach 16 * step (polling with
+// acquire loads, bounded by WAIT_LIMIT_NS: on expiry the error word gets
+// QC_ERR_TIMEOUT and the CTA returns without output), then the CTA merges
+// the records, read through L2 (they were written by other GPUs).
+__global__ void __launch_bounds__(256) attn_merge_mailbox_kernel(const MailboxMergeArgs m) {
+  __shared__ int ok;
+  const int h = blockIdx.x, t = threadIdx.x;
+  const uint32_t step = m.done[m.layer] + 1u;
+  if (t == 0) {
+    const uint32_t target = 16u * step;
+    const uint32_t* cnt = m.cnt + m.layer * m.world;
+    const uint64_t t0 = globaltimer();
+    int done = 0;
+    for (uint32_t it = 0;; ++it) {
+      done = 1;
+      for (int r = 0; r < m.world; ++r) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt + r) : "memory");
+        if ((int32_t)(v - target) < 0) { done = 0; break; }
+      }
+      if (done) break;
+      if ((it & 63u) == 0 && globaltimer() - t0 > WAIT_LIMIT_NS) {
+        record_error(m.err, QC_ERR_TIMEOUT);
+        break;
+      }
+    }
+    ok = done;
+  }
+  __syncthreads();
+  if (!ok) return;
+  const float* rec = m.rec + ((int64_t)(step & 1u) * m.n_layers + m.layer) * m.world * 16 * (HD + 2);
+  float M = -INFINITY;
+  for (int g = 0; g < m.world; ++g) M = fmaxf(M, __ldcg(rec + (g * 16 + h) * (HD + 2)));
+  float L = 0.0f, O = 0.0f;
+  for (int g = 0; g < m.world; ++g) {
+    const float* r = rec + (g * 16 + h) * (HD + 2);
+    const float mg = __ldcg(r);
+    const float f = (mg == -INFINITY) ? 0.0f : exp2f(mg - M);
+    L = fmaf(f, __ldcg(r + 1), L);
+    O = fmaf(f, __ldcg(r + 2 + t), O);
+  }
+  const float gt = bf2f(m.proj[h * 2 * HD + HD + t]);
+  m.out[h * HD + t] = f2bf((O / L) * sigmoid_exact(gt));
+  __syncthreads();
+  // every CTA read done[layer] at its start; the 16th to get here advances it
+  if (t == 0 && atomicAdd(m.consumed + m.layer, 1u) % 16u == 15u) atomicAdd(m.done + m.layer, 1u);
+}
+
 }  // namespace
+
+cudaError_t launch_attn_merge_mailbox(const MailboxMergeArgs& m, cudaStream_t s) {
+  attn_merge_mailbox_kernel<<<16, 256, 0, s>>>(m);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_attn_merge_records(const float* records, int32_t n_parts, const uint16_t* proj,
                                       uint16_t* out, cudaStream_t s) {

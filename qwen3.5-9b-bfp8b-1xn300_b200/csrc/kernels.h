@@ -78,6 +78,14 @@ struct CombineArgs {
   // when non-null: write the merged record (m, l, o unnormalised) of sequence
   // 0 as [16 heads][2 + 256] instead of the gated bf16 output
   float* record;
+  // when world > 0 (split over devices through peer memory): write the record
+  // into slot [step & 1][layer][rank] of every rank's mailbox instead, then
+  // add 1 to counter [layer][rank] of every rank (system scope); step =
+  // this rank's done[layer] + 1
+  int32_t world, rank, layer, n_layers;
+  float* mbox_rec[QC_P2P_MAX_RANKS];       // each rank's record area (peer pointers)
+  uint32_t* mbox_cnt[QC_P2P_MAX_RANKS];    // each rank's counters
+  const uint32_t* done;                    // this rank's merged steps per layer
 };
 // tmk / tmv: 2D tensor maps over this layer's K / V pool viewed as
 // [max_pages * 4 * 64 rows][256 bf16], box 16 rows x 64 columns, 128 B swizzle.
@@ -88,6 +96,20 @@ int attn_smem_bytes();
 // output [4096] of one sequence (attn_decode.cu).
 cudaError_t launch_attn_merge_records(const float* records, int32_t n_parts, const uint16_t* proj,
                                       uint16_t* out, cudaStream_t s);
+// The same merge from this rank's mailbox, after waiting (bounded) until every
+// rank's counter [layer][r] has reached 16 * (done[layer] + 1); the last CTA
+// to finish advances done[layer].
+struct MailboxMergeArgs {
+  const float* rec;        // this rank's record area [2][n_layers][world][16][258]
+  const uint32_t* cnt;     // this rank's counters [n_layers][world]
+  uint32_t* done;          // [n_layers] steps merged
+  uint32_t* consumed;      // [n_layers] CTAs finished, for advancing done
+  int32_t world, layer, n_layers;
+  const uint16_t* proj;
+  uint16_t* out;
+  int* err;
+};
+cudaError_t launch_attn_merge_mailbox(const MailboxMergeArgs& m, cudaStream_t s);
 
 // Message returned by qc_last_error(NULL) on this thread (qcache.cu).
 void set_thread_error(const char* msg);

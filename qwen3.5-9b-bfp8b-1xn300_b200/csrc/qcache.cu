@@ -84,6 +84,10 @@ struct qc_ctx {
   int32_t* page_table = nullptr;// [max_seqs][pt_stride]
   int32_t* desc = nullptr;      // batch: slots | pos | seg | page0 | append
   int32_t* desc_part = nullptr; // same layout, one sequence, for qc_attn_partial
+  // split-K over devices through peer memory (qc_p2p_*)
+  int32_t p2p_world = 0, p2p_rank = -1;
+  char* mbox = nullptr;         // this rank's mailbox (records, then counters)
+  char* peer_mbox[QC_P2P_MAX_RANKS] = {};  // every rank's mailbox, self included
   float* part_m = nullptr;
   float* part_l = nullptr;
   float* part_o = nullptr;
@@ -445,6 +449,9 @@ void qc_destroy(qc_ctx* c) {
   if (!c->host_only) {
     cudaSetDevice(c->device);
     cudaDeviceSynchronize();
+    for (int r = 0; r < c->p2p_world; ++r)
+      if (r != c->p2p_rank && c->peer_mbox[r]) cudaIpcCloseMemHandle(c->peer_mbox[r]);
+    if (c->mbox) cudaFree(c->mbox);
     void* ptrs[] = {c->k_pool, c->v_pool, c->state, c->ring, c->snap_state, c->snap_hist,
                     c->q_norm, c->k_norm, c->ssm_a, c->dt_bias, c->ssm_norm, c->conv_w,
                     c->rope_cos, c->rope_sin, c->page_table, c->desc, c->desc_part, c->pf_q, c->pf_rec, c->pf_conv,
@@ -1224,4 +1231,141 @@ int qc_attn_combine(qc_ctx* c, const float* partials, int32_t n_parts, const uin
   return QC_OK;
 }
 
+
+// Mailbox layout: records [2][n_attn_layers][world][16][258] f32, then
+// counters [n_attn_layers][world] u32 (written by every rank), then this
+// rank's own done[n_attn_layers] and consumed[n_attn_layers] u32.
+static size_t mbox_rec_bytes(const qc_ctx* c, int world) {
+  return (size_t)2 * c->cfg.n_attn_layers * world * 16 * 258 * sizeof(float);
+}
+static size_t mbox_bytes(const qc_ctx* c, int world) {
+  return mbox_rec_bytes(c, world) + (size_t)c->cfg.n_attn_layers * (world + 2) * sizeof(uint32_t);
+}
+
+int qc_p2p_create(qc_ctx* c, int32_t world, int32_t rank, void* handle_out) {
+  if (!c || !handle_out || world < 2 || world > QC_P2P_MAX_RANKS || rank < 0 || rank >= world)
+    return c ? fail(c, QC_ERR_ARG, "qc_p2p_create: world %d rank %d", world, rank) : QC_ERR_ARG;
+  QC_NEED_DEVICE(c);
+  if (c->mbox) return fail(c, QC_ERR_ARG, "qc_p2p_create: mailbox already created");
+  cudaSetDevice(c->device);
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, mbox_bytes(c, world));
+  if (e != cudaSuccess) return fail(c, QC_ERR_OOM, "qc_p2p_create: %s", cudaGetErrorString(e));
+  c->mbox = static_cast<char*>(p);
+  QC_CUDA(c, cudaMemset(c->mbox, 0, mbox_bytes(c, world)));
+  QC_CUDA(c, cudaDeviceSynchronize());
+  cudaIpcMemHandle_t h;
+  QC_CUDA(c, cudaIpcGetMemHandle(&h, c->mbox));
+  std::memcpy(handle_out, &h, sizeof(h));
+  c->p2p_world = world;
+  c->p2p_rank = rank;
+  c->peer_mbox[rank] = c->mbox;
+  return QC_OK;
+}
+
+int qc_p2p_open(qc_ctx* c, int32_t peer, const void* handle) {
+  if (!c || !handle) return QC_ERR_ARG;
+  QC_NEED_DEVICE(c);
+  if (!c->mbox) return fail(c, QC_ERR_ARG, "qc_p2p_open: call qc_p2p_create first");
+  if (peer < 0 || peer >= c->p2p_world || peer == c->p2p_rank)
+    return fail(c, QC_ERR_ARG, "qc_p2p_open: peer %d", peer);
+  if (c->peer_mbox[peer]) return fail(c, QC_ERR_ARG, "qc_p2p_open: peer %d already open", peer);
+  cudaSetDevice(c->device);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  QC_CUDA(c, cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  c->peer_mbox[peer] = static_cast<char*>(p);
+  return QC_OK;
+}
+
+static uint32_t* mbox_done(qc_ctx* c) {
+  return reinterpret_cast<uint32_t*>(c->mbox + mbox_rec_bytes(c, c->p2p_world)) +
+         (size_t)c->cfg.n_attn_layers * c->p2p_world;
+}
+
+static int p2p_ready(qc_ctx* c) {
+  if (!c->mbox) return fail(c, QC_ERR_ARG, "no peer mailbox (qc_p2p_create)");
+  for (int r = 0; r < c->p2p_world; ++r)
+    if (!c->peer_mbox[r]) return fail(c, QC_ERR_ARG, "peer %d not opened (qc_p2p_open)", r);
+  return QC_OK;
+}
+
+int qc_attn_partial_p2p(qc_ctx* c, int layer, const uint16_t* proj, qc_stream stream) {
+  qc::TraceRange trace_("qc_attn_partial_p2p");
+  if (!c || !proj) return QC_ERR_ARG;
+  if (!c->in_step) return fail(c, QC_ERR_ARG, "no open decode step");
+  if (c->b_seq.size() != 1) return fail(c, QC_ERR_ARG, "split-K needs a batch of 1");
+  if (layer < 0 || layer >= c->cfg.n_attn_layers) return fail(c, QC_ERR_ARG, "attn layer %d", layer);
+  QC_NEED_DEVICE(c);
+  int rc = p2p_ready(c);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t base = (int64_t)layer * c->cfg.max_pages * PAGE_ELEMS;
+  qc::AttnArgs a{};
+  a.proj = proj;
+  a.k_pool = c->k_pool + base;
+  a.v_pool = c->v_pool + base;
+  a.page_table = c->page_table;
+  a.pt_stride = c->pt_stride;
+  a.max_pages = c->cfg.max_pages;
+  a.slots = c->desc_part;
+  a.pos = c->desc_part + 1;
+  a.seg = c->desc_part + 2;
+  a.page0 = c->desc_part + 4;
+  a.append = c->desc_part + 5;
+  a.split = c->desc_part + 6;
+  a.q_norm = c->q_norm + layer * HD;
+  a.k_norm = c->k_norm + layer * HD;
+  a.rope_cos = c->rope_cos;
+  a.rope_sin = c->rope_sin;
+  a.part_m = c->part_m;
+  a.part_l = c->part_l;
+  a.part_o = c->part_o;
+  a.n = 1;
+  a.grid = c->nsm;
+  a.err = c->dev_err;
+  qc::CombineArgs cb{};
+  cb.proj = proj;
+  cb.seg = a.seg;
+  cb.part_m = c->part_m;
+  cb.part_l = c->part_l;
+  cb.part_o = c->part_o;
+  cb.split = a.split;
+  cb.n = 1;
+  cb.world = c->p2p_world;
+  cb.rank = c->p2p_rank;
+  cb.layer = layer;
+  cb.n_layers = c->cfg.n_attn_layers;
+  for (int r = 0; r < c->p2p_world; ++r) {
+    cb.mbox_rec[r] = reinterpret_cast<float*>(c->peer_mbox[r]);
+    cb.mbox_cnt[r] = reinterpret_cast<uint32_t*>(c->peer_mbox[r] + mbox_rec_bytes(c, c->p2p_world));
+  }
+  cb.done = mbox_done(c);
+  QC_CUDA(c, qc::launch_attn_decode(a, cb, c->tm_k[layer], c->tm_v[layer], st));
+  return QC_OK;
+}
+
+int qc_attn_combine_p2p(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out,
+                        qc_stream stream) {
+  qc::TraceRange trace_("qc_attn_combine_p2p");
+  if (!c || !proj || !out) return QC_ERR_ARG;
+  if (layer < 0 || layer >= c->cfg.n_attn_layers) return fail(c, QC_ERR_ARG, "attn layer %d", layer);
+  QC_NEED_DEVICE(c);
+  int rc = p2p_ready(c);
+  if (rc) return rc;
+  qc::MailboxMergeArgs m{};
+  m.rec = reinterpret_cast<const float*>(c->mbox);
+  m.cnt = reinterpret_cast<const uint32_t*>(c->mbox + mbox_rec_bytes(c, c->p2p_world));
+  m.done = mbox_done(c);
+  m.consumed = mbox_done(c) + c->cfg.n_attn_layers;
+  m.world = c->p2p_world;
+  m.layer = layer;
+  m.n_layers = c->cfg.n_attn_layers;
+  m.proj = proj;
+  m.out = out;
+  m.err = c->dev_err;
+  QC_CUDA(c, qc::launch_attn_merge_mailbox(m, (cudaStream_t)stream));
+  return QC_OK;
+}
 }  // extern "C"

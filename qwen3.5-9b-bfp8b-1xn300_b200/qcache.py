@@ -106,6 +106,10 @@ def lib() -> C.CDLL:
         "qc_attn_partial_range": (C.c_int, [P, I32, I32, I32, P]),
         "qc_attn_partial": (C.c_int, [P, C.c_int, P, P, P]),
         "qc_attn_combine": (C.c_int, [P, P, I32, P, P, P]),
+        "qc_p2p_create": (C.c_int, [P, I32, I32, P]),
+        "qc_p2p_open": (C.c_int, [P, I32, P]),
+        "qc_attn_partial_p2p": (C.c_int, [P, C.c_int, P, P]),
+        "qc_attn_combine_p2p": (C.c_int, [P, C.c_int, P, P, P]),
         "qc_attn_decode_noalloc": (C.c_int, [P, P, P, I32, P, I32, PI32, I32, P, P, P, P, P, P]),
         "qc_bfp8_packed_bytes": (C.c_int64, [I32, I32]),
         "qc_bfp8_create": (C.c_int, [C.c_int, I32, I32, C.POINTER(P)]),
@@ -295,6 +299,22 @@ class QCache:
 
     def attn_partial(self, layer, proj_ptr, partial_ptr, stream=0):
         self._ck(self.L.qc_attn_partial(self.h, layer, proj_ptr, partial_ptr, stream))
+
+    def p2p_create(self, world, rank) -> bytes:
+        """Allocates the peer mailbox; returns its IPC handle for the peers."""
+        buf = (C.c_char * 64)()
+        self._ck(self.L.qc_p2p_create(self.h, world, rank, buf))
+        return bytes(buf)
+
+    def p2p_open(self, peer, handle: bytes):
+        buf = (C.c_char * 64).from_buffer_copy(handle)
+        self._ck(self.L.qc_p2p_open(self.h, peer, buf))
+
+    def attn_partial_p2p(self, layer, proj_ptr, stream=0):
+        self._ck(self.L.qc_attn_partial_p2p(self.h, layer, proj_ptr, stream))
+
+    def attn_combine_p2p(self, layer, proj_ptr, out_ptr, stream=0):
+        self._ck(self.L.qc_attn_combine_p2p(self.h, layer, proj_ptr, out_ptr, stream))
 
     def attn_combine(self, partials_ptr, n_parts, proj_ptr, out_ptr, stream=0):
         self._ck(self.L.qc_attn_combine(self.h, partials_ptr, n_parts, proj_ptr, out_ptr, stream))
