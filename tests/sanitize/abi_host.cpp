@@ -104,6 +104,13 @@ int main() {
   EXPECT(qc_prefix_release(q, e) == QC_OK);
   EXPECT(qc_prefix_release(q, 1234) != QC_OK);
 
+  // peer-memory split-K needs a device; bad ranks are rejected first
+  char handle[QC_P2P_HANDLE_BYTES];
+  EXPECT(qc_p2p_create(q, 2, 0, handle) == QC_ERR_NODEVICE);
+  EXPECT(qc_p2p_create(q, 1, 0, handle) == QC_ERR_ARG);
+  EXPECT(qc_p2p_open(q, 1, handle) == QC_ERR_NODEVICE);
+  EXPECT(qc_attn_combine_p2p(q, 0, nullptr, nullptr, nullptr) == QC_ERR_ARG);
+
   // the other headers' entry points reject missing arguments
   EXPECT(qc_bfp8_gemv(nullptr, nullptr, 1, nullptr, nullptr) == QC_ERR_ARG);
   EXPECT(qc_bfp8_packed_bytes(33, 32) == -1);

@@ -38,6 +38,12 @@ def test_device_calls_fail_loudly_on_host_only(qcache):
     with pytest.raises(qcache.QCacheError) as e:
         q.gdn_decode(0, 16, 16)
     assert e.value.code == qcache.QC_ERR_NODEVICE
+    with pytest.raises(qcache.QCacheError) as e:
+        q.p2p_create(2, 0)
+    assert e.value.code == qcache.QC_ERR_NODEVICE
+    with pytest.raises(qcache.QCacheError) as e:
+        q.attn_combine_p2p(0, 16, 16)
+    assert e.value.code == qcache.QC_ERR_NODEVICE
 
 
 def test_sequence_slots_and_pages(qcache):
