@@ -187,14 +187,27 @@ class Stack:
                 hi = torch.randn(3, 8192, generator=g, device="cuda").to(bf16)
                 q.gdn_state_write(s, l, st.data_ptr(), hi.data_ptr(), stream)
                 torch.cuda.synchronize()
-        # per-layer projection inputs and outputs
-        self.proj = []
-        for kind in kinds:
-            w = 10240 if kind == "a" else 12352
-            self.proj.append(torch.randn(n, w, generator=g, device="cuda").to(bf16))
-        self.out = [torch.empty(n, 4096, device="cuda", dtype=bf16) for _ in kinds]
+        # per-layer projection inputs and outputs: views into one contiguous
+        # buffer each, so a step's inputs (outputs) move in one copy
+        self.proj_flat, self.proj = Stack.layer_views(torch, kinds, n, bf16)
+        self.proj_flat.copy_(torch.randn(self.proj_flat.numel(), generator=g, device="cuda"))
+        self.out_flat = torch.empty(len(kinds) * n * 4096, device="cuda", dtype=bf16)
+        self.out = [self.out_flat[i * n * 4096:(i + 1) * n * 4096].view(n, 4096)
+                    for i in range(len(kinds))]
         torch.cuda.synchronize()
         q.check_device()
+
+    @staticmethod
+    def layer_views(torch, kinds, n, dtype):
+        """One flat device buffer holding every layer's [n][row] projection
+        input, and the per-layer views into it."""
+        widths = [10240 if kd == "a" else 12352 for kd in kinds]
+        flat = torch.empty(n * sum(widths), device="cuda", dtype=dtype)
+        views, off = [], 0
+        for w in widths:
+            views.append(flat[off:off + n * w].view(n, w))
+            off += n * w
+        return flat, views
 
     def step(self, events=None):
         self.q.decode_begin(self.seqs, stream=self.stream)
@@ -251,7 +264,7 @@ def run_ours(args, rank, world, dist, kinds, n_total, ctx):
     torch.cuda.set_device(local)
     n = n_total // world
     stream = torch.cuda.current_stream().cuda_stream
-    stack = Stack(qc, synth, torch, kinds, n, ctx, args.warmup + args.steps + 8,
+    stack = Stack(qc, synth, torch, kinds, n, ctx, args.warmup + 2 * args.steps + 8,
                   seed=1000 + rank, stream=stream)
     nl = len(kinds)
     # inputs smaller than L2 (126 MB): flush it between steps, outside the events
@@ -334,13 +347,15 @@ def run_ours(args, rank, world, dist, kinds, n_total, ctx):
     # buffer sets, two captured graphs and two copy streams pipeline the
     # transfers of step k + 1 (inputs) and k - 1 (outputs) under step k.
     bf16 = torch.bfloat16
-    h_in = [torch.empty(p.shape, dtype=bf16, pin_memory=True).copy_(p.cpu()) for p in stack.proj]
-    h_out = [torch.empty(o.shape, dtype=bf16, pin_memory=True) for o in stack.out]
-    h2d = sum(t.numel() * 2 for t in h_in)
-    d2h = sum(t.numel() * 2 for t in h_out)
-    sets = [(stack.proj, stack.out, graph)]
-    proj2 = [torch.empty_like(p) for p in stack.proj]
-    out2 = [torch.empty_like(o) for o in stack.out]
+    h_in = torch.empty(stack.proj_flat.shape, dtype=bf16, pin_memory=True).copy_(
+        stack.proj_flat.cpu())
+    h_out = torch.empty(stack.out_flat.shape, dtype=bf16, pin_memory=True)
+    h2d = h_in.numel() * 2
+    d2h = h_out.numel() * 2
+    sets = [(stack.proj_flat, stack.out_flat, graph)]
+    proj2_flat, proj2 = Stack.layer_views(torch, kinds, n, bf16)
+    out2_flat = torch.empty_like(stack.out_flat)
+    out2 = [out2_flat[i * n * 4096:(i + 1) * n * 4096].view(n, 4096) for i in range(len(kinds))]
     saved = (stack.proj, stack.out)
     stack.proj, stack.out = proj2, out2
     graph2 = torch.cuda.CUDAGraph()
@@ -350,7 +365,7 @@ def run_ours(args, rank, world, dist, kinds, n_total, ctx):
         stack.layers(torch.cuda.current_stream().cuda_stream)
     stack.q.decode_abort()
     stack.proj, stack.out = saved
-    sets.append((proj2, out2, graph2))
+    sets.append((proj2_flat, out2_flat, graph2))
     torch.cuda.synchronize()
     main = torch.cuda.current_stream()
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
@@ -362,11 +377,12 @@ def run_ours(args, rank, world, dist, kinds, n_total, ctx):
         with torch.cuda.stream(s_in):
             if wait_done:
                 s_in.wait_event(ev_done[b])
-            for p, h in zip(sets[b][0], h_in):
-                p.copy_(h, non_blocking=True)
+            sets[b][0].copy_(h_in, non_blocking=True)
             ev_in[b].record(s_in)
 
-    e2e_steps = max(2, min(args.steps, 10))
+    # every step copies its inputs in and its outputs out; the first load and
+    # the last drain are inside the timed region too
+    e2e_steps = max(2, args.steps)
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -385,8 +401,7 @@ def run_ours(args, rank, world, dist, kinds, n_total, ctx):
         ev_done[b].record(main)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_done[b])
-            for o, h in zip(sets[b][1], h_out):
-                h.copy_(o, non_blocking=True)
+            h_out.copy_(sets[b][1], non_blocking=True)
             ev_out[b].record(s_out)
     main.wait_event(ev_out[(e2e_steps - 1) % 2])
     e1.record(main)
