@@ -736,8 +736,17 @@ def run_gemv(args, batches=(1, 8, 16)):
     stream = torch.cuda.Stream()
     res = {}
     for B in batches:
-        xs = [torch.randn(B, K, generator=g, device="cuda").to(torch.bfloat16) for _, K in shapes]
-        ys = [torch.empty(B, M, device="cuda", dtype=torch.bfloat16) for M, _ in shapes]
+        # every GEMV's activations (outputs) are views into one buffer, so a
+        # step's inputs (outputs) move in one copy
+        x_flat = torch.randn(B * sum(K for _, K in shapes), generator=g, device="cuda").to(
+            torch.bfloat16)
+        y_flat = torch.empty(B * sum(M for M, _ in shapes), device="cuda", dtype=torch.bfloat16)
+        xs, ys, ox, oy = [], [], 0, 0
+        for M, K in shapes:
+            xs.append(x_flat[ox:ox + B * K].view(B, K))
+            ys.append(y_flat[oy:oy + B * M].view(B, M))
+            ox += B * K
+            oy += B * M
 
         def step(st):
             for m, x, y in zip(mats, xs, ys):
@@ -773,22 +782,20 @@ def run_gemv(args, batches=(1, 8, 16)):
             stream.synchronize()
             one_ms = f0.elapsed_time(f1) / reps
             # e2e: activations in from pinned host memory, outputs back out
-            hx = [torch.empty_like(x, device="cpu").pin_memory() for x in xs]
-            hy = [torch.empty_like(y, device="cpu").pin_memory() for y in ys]
+            hx = torch.empty_like(x_flat, device="cpu").pin_memory()
+            hy = torch.empty_like(y_flat, device="cpu").pin_memory()
             stream.synchronize()
             t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             t0.record(stream)
             for _ in range(args.steps):
-                for x, h in zip(xs, hx):
-                    x.copy_(h, non_blocking=True)
+                x_flat.copy_(hx, non_blocking=True)
                 graph.replay()
-                for y, h in zip(ys, hy):
-                    h.copy_(y, non_blocking=True)
+                hy.copy_(y_flat, non_blocking=True)
             t1.record(stream)
             stream.synchronize()
             e2e_ms = t0.elapsed_time(t1) / args.steps
         res[B] = dict(ms=ms, one_ms=one_ms, big=shapes[big], clocks=clocks, e2e_ms=e2e_ms,
-                      h2d=sum(x.numel() * 2 for x in xs), d2h=sum(y.numel() * 2 for y in ys))
+                      h2d=x_flat.numel() * 2, d2h=y_flat.numel() * 2)
     for m in mats:
         m.check()
     return res, tile_bytes
