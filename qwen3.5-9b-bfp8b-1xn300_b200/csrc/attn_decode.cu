@@ -52,6 +52,7 @@ constexpr int BOX_ROWS = 16;              // TMA box: 16 rows x 64 bf16 (2 KiB)
 constexpr int BOX_BYTES = BOX_ROWS * 128;
 // score * 1/16 (src/model_config.h:40), kept in the log2 domain for exp2
 constexpr float SCALE_LOG2 = 0.0625f * 1.4426950408889634f;
+constexpr float RESCALE_SLACK = 8.0f;      // log2 of the largest unnormalised weight
 
 struct __align__(1024) Smem {
   uint16_t k[STAGES][TILE_ELEMS];   // swizzled: [col block 4][row 64][128 B]
@@ -439,9 +440,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         mx0 = fmaxf(mx0, __shfl_xor_sync(FULL_MASK, mx0, m));
         mx1 = fmaxf(mx1, __shfl_xor_sync(FULL_MASK, mx1, m));
       }
-      const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
-      const float c0 = (mn0 == -INFINITY) ? 1.0f : exp2f(m_run[0] - mn0);
-      const float c1 = (mn1 == -INFINITY) ? 1.0f : exp2f(m_run[1] - mn1);
+      // Lazy reference maximum: it moves only when a score exceeds it by more
+      // than 2^RESCALE_SLACK, so p <= 2^RESCALE_SLACK and most tiles skip the
+      // rescale of the accumulators.  (m, l, o) stays consistent either way:
+      // o / l is the same softmax average.
+      const bool up0 = mx0 > m_run[0] + RESCALE_SLACK, up1 = mx1 > m_run[1] + RESCALE_SLACK;
+      const float mn0 = up0 ? mx0 : m_run[0], mn1 = up1 ? mx1 : m_run[1];
+      const float c0 = up0 ? exp2f(m_run[0] - mn0) : 1.0f;
+      const float c1 = up1 ? exp2f(m_run[1] - mn1) : 1.0f;
       const float p0 = (sc0 == -INFINITY) ? 0.0f : exp2f(sc0 - mn0);
       const float p1 = (sc1 == -INFINITY) ? 0.0f : exp2f(sc1 - mn1);
       float ps0 = p0, ps1 = p1;
@@ -454,12 +460,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       l_run[1] = fmaf(l_run[1], c1, ps1);
       m_run[0] = mn0;
       m_run[1] = mn1;
+      if (__any_sync(FULL_MASK, up0 || up1)) {
 #pragma unroll
-      for (int mt = 0; mt < 16; ++mt) {
-        oacc[mt][0] *= c0;
-        oacc[mt][1] *= c1;
-        oacc[mt][2] *= c0;
-        oacc[mt][3] *= c1;
+        for (int mt = 0; mt < 16; ++mt) {
+          oacc[mt][0] *= c0;
+          oacc[mt][1] *= c1;
+          oacc[mt][2] *= c0;
+          oacc[mt][3] *= c1;
+        }
       }
       // ---- Px^T B fragment: matrix [pos g][col], col 2t4, 2t4+1 = hi (t4 < 2)
       // or lo (t4 >= 2) parts of p for heads hA, hA + 1; transpose with movmatrix
