@@ -276,6 +276,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int mt = 0; mt < 16; ++mt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) oacc[mt][e] += __shfl_xor_sync(FULL_MASK, oacc[mt][e], 2);
+#pragma unroll
+    for (int m = 4; m <= 16; m <<= 1) {  // per-lane l -> the warp's l per head
+      l_run[0] += __shfl_xor_sync(FULL_MASK, l_run[0], m);
+      l_run[1] += __shfl_xor_sync(FULL_MASK, l_run[1], m);
+    }
     if (lane < 2) {
       sm.red_ml[warp][2 * lane] = m_run[0];
       sm.red_ml[warp][2 * lane + 1] = m_run[1];
@@ -434,33 +439,33 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool valid = (r0 + g) < t.tile_len;
       const float sc0 = valid ? s0 * SCALE_LOG2 : -INFINITY;
       const float sc1 = valid ? s1 * SCALE_LOG2 : -INFINITY;
-      float mx0 = sc0, mx1 = sc1;
-#pragma unroll
-      for (int m = 4; m <= 16; m <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(FULL_MASK, mx0, m));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(FULL_MASK, mx1, m));
-      }
       // Lazy reference maximum: it moves only when a score exceeds it by more
-      // than 2^RESCALE_SLACK, so p <= 2^RESCALE_SLACK and most tiles skip the
-      // rescale of the accumulators.  (m, l, o) stays consistent either way:
-      // o / l is the same softmax average.
-      const bool up0 = mx0 > m_run[0] + RESCALE_SLACK, up1 = mx1 > m_run[1] + RESCALE_SLACK;
-      const float mn0 = up0 ? mx0 : m_run[0], mn1 = up1 ? mx1 : m_run[1];
-      const float c0 = up0 ? exp2f(m_run[0] - mn0) : 1.0f;
-      const float c1 = up1 ? exp2f(m_run[1] - mn1) : 1.0f;
-      const float p0 = (sc0 == -INFINITY) ? 0.0f : exp2f(sc0 - mn0);
-      const float p1 = (sc1 == -INFINITY) ? 0.0f : exp2f(sc1 - mn1);
-      float ps0 = p0, ps1 = p1;
+      // than 2^RESCALE_SLACK, so p <= 2^RESCALE_SLACK and most tiles need
+      // neither the max reduction over the warp's positions nor the rescale
+      // of the accumulators.  (m, l, o) stays consistent either way: o / l is
+      // the same softmax average.
+      bool up0 = sc0 > m_run[0] + RESCALE_SLACK, up1 = sc1 > m_run[1] + RESCALE_SLACK;
+      const bool rescale = __any_sync(FULL_MASK, up0 || up1);
+      float c0 = 1.0f, c1 = 1.0f;
+      if (rescale) {
+        float mx0 = sc0, mx1 = sc1;
 #pragma unroll
-      for (int m = 4; m <= 16; m <<= 1) {
-        ps0 += __shfl_xor_sync(FULL_MASK, ps0, m);
-        ps1 += __shfl_xor_sync(FULL_MASK, ps1, m);
+        for (int m = 4; m <= 16; m <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(FULL_MASK, mx0, m));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(FULL_MASK, mx1, m));
+        }
+        up0 = mx0 > m_run[0] + RESCALE_SLACK;
+        up1 = mx1 > m_run[1] + RESCALE_SLACK;
+        if (up0) { c0 = exp2f(m_run[0] - mx0); m_run[0] = mx0; }
+        if (up1) { c1 = exp2f(m_run[1] - mx1); m_run[1] = mx1; }
       }
-      l_run[0] = fmaf(l_run[0], c0, ps0);
-      l_run[1] = fmaf(l_run[1], c1, ps1);
-      m_run[0] = mn0;
-      m_run[1] = mn1;
-      if (__any_sync(FULL_MASK, up0 || up1)) {
+      const float p0 = (sc0 == -INFINITY) ? 0.0f : exp2f(sc0 - m_run[0]);
+      const float p1 = (sc1 == -INFINITY) ? 0.0f : exp2f(sc1 - m_run[1]);
+      // l is kept per lane (this lane's positions) and summed over the warp
+      // at the flush
+      l_run[0] = fmaf(l_run[0], c0, p0);
+      l_run[1] = fmaf(l_run[1], c1, p1);
+      if (rescale) {
 #pragma unroll
         for (int mt = 0; mt < 16; ++mt) {
           oacc[mt][0] *= c0;
