@@ -8,7 +8,7 @@
 // chunk in parallel, the causal conv + SiLU of the head's q and k channels and
 // of the CTA's v channels (history from the conv ring, then the chunk's own
 // inputs), the L2 norms, decay and beta.  Phase B keeps the CTA's rows of the
-// fp32 state in registers (2 rows per warp, one float4 per lane and row) and
+// fp32 state in registers (one row per half-warp, two float4 per lane) and
 // runs the delta rule token after token — the state is read from and written
 // to HBM once per chunk instead of once per token.  Phase C applies
 // the gated RMSNorm per token.
@@ -133,58 +133,53 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArg
   }
   __syncthreads();
 
-  // ---- phase B: delta rule token by token, this warp's rows in registers
-  const int row0 = warp * GRPW;  // local row
+  // ---- phase B: delta rule token by token, this warp's rows in registers:
+  // half-warp h owns local row row0 + h, lane j of the half holds dims
+  // 4j..4j+3 and 64+4j..64+4j+3, so each row's dot products reduce over 16
+  // lanes (4 butterfly levels for both sums, 8 shuffles per token)
+  static_assert(GRPW == 2, "one row per half-warp");
+  const int hw = lane >> 4, j = lane & 15;
+  const int row = warp * GRPW + hw;  // local row
   float* st = a.state + (int64_t)vh * HK * HK + (int64_t)r * GRB * HK;
-  float4 S[GRPW];
-#pragma unroll
-  for (int i = 0; i < GRPW; ++i) S[i] = reinterpret_cast<const float4*>(st)[(row0 + i) * 32 + lane];
+  float4* srow = reinterpret_cast<float4*>(st) + row * 32;
+  float4 S0 = srow[j], S1 = srow[j + 16];
   // Per token both dot products read the state before the token: with
   // sk = decay (S.k), d = beta (v - sk) and S' = decay S + d k^T, the
   // output is S'.q = decay (S.q) + d (k.q) — one reduction tree per token
   // instead of two in sequence.
   for (int t = 0; t < T; ++t) {
-    const float4 k4 = reinterpret_cast<const float4*>(sm.k[t])[lane];
-    const float4 q4 = reinterpret_cast<const float4*>(sm.q[t])[lane];
-    const float dec = sm.decay[t], bt = sm.beta[t], kq = sm.kq[t];
-    float sk[GRPW], sq[GRPW];
+    const float4 ka = reinterpret_cast<const float4*>(sm.k[t])[j];
+    const float4 kb = reinterpret_cast<const float4*>(sm.k[t])[j + 16];
+    const float4 qa = reinterpret_cast<const float4*>(sm.q[t])[j];
+    const float4 qb = reinterpret_cast<const float4*>(sm.q[t])[j + 16];
+    const float dec = sm.decay[t], bt = sm.beta[t], kq = sm.kq[t], vv = sm.v[t][row];
+    float sk = S0.x * ka.x, sk2 = S1.x * kb.x, sq = S0.x * qa.x, sq2 = S1.x * qb.x;
+    sk = fmaf(S0.y, ka.y, sk);  sk2 = fmaf(S1.y, kb.y, sk2);
+    sq = fmaf(S0.y, qa.y, sq);  sq2 = fmaf(S1.y, qb.y, sq2);
+    sk = fmaf(S0.z, ka.z, sk);  sk2 = fmaf(S1.z, kb.z, sk2);
+    sq = fmaf(S0.z, qa.z, sq);  sq2 = fmaf(S1.z, qb.z, sq2);
+    sk = fmaf(S0.w, ka.w, sk);  sk2 = fmaf(S1.w, kb.w, sk2);
+    sq = fmaf(S0.w, qa.w, sq);  sq2 = fmaf(S1.w, qb.w, sq2);
+    sk += sk2;
+    sq += sq2;
 #pragma unroll
-    for (int i = 0; i < GRPW; ++i) {
-      float d = S[i].x * k4.x;
-      d = fmaf(S[i].y, k4.y, d);
-      d = fmaf(S[i].z, k4.z, d);
-      sk[i] = fmaf(S[i].w, k4.w, d);
-      float e = S[i].x * q4.x;
-      e = fmaf(S[i].y, q4.y, e);
-      e = fmaf(S[i].z, q4.z, e);
-      sq[i] = fmaf(S[i].w, q4.w, e);
+    for (int m = 8; m >= 1; m >>= 1) {
+      sk += __shfl_xor_sync(FULL_MASK, sk, m);
+      sq += __shfl_xor_sync(FULL_MASK, sq, m);
     }
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1)
-#pragma unroll
-      for (int i = 0; i < GRPW; ++i) {
-        sk[i] += __shfl_xor_sync(FULL_MASK, sk[i], m);
-        sq[i] += __shfl_xor_sync(FULL_MASK, sq[i], m);
-      }
-    float o[GRPW];
-#pragma unroll
-    for (int i = 0; i < GRPW; ++i) {
-      const float dd = bt * (sm.v[t][row0 + i] - dec * sk[i]);
-      S[i].x = fmaf(k4.x, dd, S[i].x * dec);
-      S[i].y = fmaf(k4.y, dd, S[i].y * dec);
-      S[i].z = fmaf(k4.z, dd, S[i].z * dec);
-      S[i].w = fmaf(k4.w, dd, S[i].w * dec);
-      o[i] = fmaf(dd, kq, dec * sq[i]);
-    }
-    if (lane < GRPW) {
-      float ov = o[0];
-#pragma unroll
-      for (int i = 1; i < GRPW; ++i) ov = (lane == i) ? o[i] : ov;
-      sm.o[t][row0 + lane] = ov * SSM_SCALE;
-    }
+    const float dd = bt * (vv - dec * sk);
+    S0.x = fmaf(ka.x, dd, S0.x * dec);
+    S0.y = fmaf(ka.y, dd, S0.y * dec);
+    S0.z = fmaf(ka.z, dd, S0.z * dec);
+    S0.w = fmaf(ka.w, dd, S0.w * dec);
+    S1.x = fmaf(kb.x, dd, S1.x * dec);
+    S1.y = fmaf(kb.y, dd, S1.y * dec);
+    S1.z = fmaf(kb.z, dd, S1.z * dec);
+    S1.w = fmaf(kb.w, dd, S1.w * dec);
+    if (j == 0) sm.o[t][row] = fmaf(dd, kq, dec * sq) * SSM_SCALE;
   }
-#pragma unroll
-  for (int i = 0; i < GRPW; ++i) reinterpret_cast<float4*>(st)[(row0 + i) * 32 + lane] = S[i];
+  srow[j] = S0;
+  srow[j + 16] = S1;
   __syncthreads();
 
   // ---- phase C: gated RMSNorm per token (src/engine.cpp:3307-3322); the
