@@ -262,12 +262,62 @@ struct PSmem {
   float red[3 * PCONSUMERS];  // q norm | k norm | output sum of squares
   uint64_t full[PSTAGES];
   uint64_t empty[PSTAGES];
+  // the next item's prologue inputs, fetched with cp.async while the current
+  // item streams: channel i < 384 is q (i < 128), k, then v of the head
+  __align__(16) float w[4][3 * HK];     // conv taps
+  __align__(16) uint16_t hist[3][3 * HK];  // conv ring, oldest tap first
+  __align__(16) uint16_t x[4 * HK];     // new inputs of the channels, then z
+  uint32_t ab[2];                        // words holding alpha and beta
 };
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+
+// Issues (does not wait for) the copies of item u's prologue inputs into
+// sm.w / sm.hist / sm.x / sm.ab; every 16-byte run is 16-byte aligned when
+// proj, the ring and the conv weights are (checked at launch).
+__device__ __forceinline__ void prefetch_item(PSmem& sm, const GdnArgs& a, int u, int tid) {
+  constexpr int NT = PCONSUMERS * 32;
+  const int b = u >> 5, vh = u & 31, kh = vh & 15;
+  const int pos = a.pos[b];
+  const uint16_t* ring = a.ring + a.slots[b] * a.ring_stride;
+  const uint16_t* x = a.proj + (int64_t)b * 12352;
+  // run r (0..2) of 128 channels: q, k, v; run 3 of x is z
+  auto chan0 = [&](int r) { return r == 0 ? kh * HK : r == 1 ? 2048 + kh * HK : 4096 + vh * HK; };
+  // 16-byte pieces: w 4 taps x 3 runs x 32, ring 3 taps x 3 runs x 16, x 4 runs x 16
+  constexpr int NW = 4 * 3 * 32, NH = 3 * 3 * 16, NX = 4 * 16;
+  for (int k = tid; k < NW + NH + NX; k += NT) {
+    if (k < NW) {
+      const int tap = k / 96, r = (k / 32) % 3, e = k % 32;
+      cp_async16(&sm.w[tap][r * HK + 4 * e], a.conv_w + tap * CONV + chan0(r) + 4 * e);
+    } else if (k < NW + NH) {
+      const int kk = k - NW, tap = kk / 48, r = (kk / 16) % 3, e = kk % 16;
+      const int slot = (pos - 3 + tap) & 3;
+      cp_async16(&sm.hist[tap][r * HK + 8 * e], ring + slot * CONV + chan0(r) + 8 * e);
+    } else {
+      const int kk = k - NW - NH, r = kk / 16, e = kk % 16;
+      const int c0 = r < 3 ? chan0(r) : Z_OFF + vh * HK;
+      cp_async16(&sm.x[r * HK + 8 * e], x + c0 + 8 * e);
+    }
+  }
+  if (tid < 2) {
+    const int off = (tid == 0 ? A_OFF : B_OFF) + vh;  // the bf16 is half of this word
+    cp_async4(&sm.ab[tid], x + (off & ~1));
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
 
 __device__ __forceinline__ void pconsumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(PCONSUMERS * 32) : "memory");
 }
 
+template <bool PRE>
 __global__ void __launch_bounds__(PTHREADS, QC_GDN_CTAS) gdn_decode_persistent(const GdnArgs a) {
   extern __shared__ __align__(128) unsigned char praw[];
   PSmem& sm = *reinterpret_cast<PSmem*>(praw);
@@ -302,6 +352,7 @@ __global__ void __launch_bounds__(PTHREADS, QC_GDN_CTAS) gdn_decode_persistent(c
   bool aborted = false;
   int i = 0;
   const float* w = a.conv_w;
+  if (PRE && blockIdx.x < n_items) prefetch_item(sm, a, blockIdx.x, tid);
   for (int u = blockIdx.x; u < n_items; u += gridDim.x) {
     const int b = u >> 5, vh = u & 31, kh = vh & 15;
     const int slot = a.slots[b], pos = a.pos[b];
@@ -309,28 +360,49 @@ __global__ void __launch_bounds__(PTHREADS, QC_GDN_CTAS) gdn_decode_persistent(c
     const uint16_t* x = a.proj + (int64_t)b * 12352;
     float* st = a.state + slot * a.state_stride + (int64_t)vh * HK * HK;
     const int t0 = (pos - 3) & 3, t1 = (pos - 2) & 3, t2 = (pos - 1) & 3, tw = pos & 3;
-    auto conv1 = [&](int c) -> float {
-      float y = bf2f(ring[t0 * CONV + c]) * w[c];
-      y = fmaf(bf2f(ring[t1 * CONV + c]), w[CONV + c], y);
-      y = fmaf(bf2f(ring[t2 * CONV + c]), w[2 * CONV + c], y);
-      y = fmaf(bf2f(x[c]), w[3 * CONV + c], y);
+    // channel c of the head, local index li (q 0..127, k 128..255, v 256..383)
+    auto conv1 = [&](int c, int li) -> float {
+      float y;
+      if (PRE) {
+        y = bf2f(sm.hist[0][li]) * sm.w[0][li];
+        y = fmaf(bf2f(sm.hist[1][li]), sm.w[1][li], y);
+        y = fmaf(bf2f(sm.hist[2][li]), sm.w[2][li], y);
+        y = fmaf(bf2f(sm.x[li]), sm.w[3][li], y);
+      } else {
+        y = bf2f(ring[t0 * CONV + c]) * w[c];
+        y = fmaf(bf2f(ring[t1 * CONV + c]), w[CONV + c], y);
+        y = fmaf(bf2f(ring[t2 * CONV + c]), w[2 * CONV + c], y);
+        y = fmaf(bf2f(x[c]), w[3 * CONV + c], y);
+      }
       return silu_exact(y);
     };
+    if (PRE) {
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      pconsumer_sync();
+    }
     // ---- prologue: conv + SiLU of the head's q, k and v channels
     constexpr int NT = PCONSUMERS * 32;
     float sq = 0.0f, sk = 0.0f;
     for (int i = tid; i < 2 * HK; i += NT) {
       const int c = (i < HK) ? kh * HK + i : 2048 + kh * HK + (i - HK);
-      const float y = conv1(c);
-      if (vh < 16) ring[tw * CONV + c] = x[c];
+      const float y = conv1(c, i);
+      if (vh < 16) ring[tw * CONV + c] = PRE ? sm.x[i] : x[c];
       if (i < HK) { sm.q[i] = y; sq = fmaf(y, y, sq); }
       else { sm.k[i - HK] = y; sk = fmaf(y, y, sk); }
     }
     for (int i = tid; i < HK; i += NT) {
       const int cv = 4096 + vh * HK + i;
-      sm.v[i] = conv1(cv);
-      ring[tw * CONV + cv] = x[cv];
-      sm.z[i] = bf2f(x[Z_OFF + vh * HK + i]);
+      sm.v[i] = conv1(cv, 2 * HK + i);
+      ring[tw * CONV + cv] = PRE ? sm.x[2 * HK + i] : x[cv];
+      sm.z[i] = bf2f(PRE ? sm.x[3 * HK + i] : x[Z_OFF + vh * HK + i]);
+    }
+    uint16_t a_raw, b_raw;
+    if (PRE) {
+      a_raw = uint16_t(sm.ab[0] >> (((A_OFF + vh) & 1) * 16));
+      b_raw = uint16_t(sm.ab[1] >> (((B_OFF + vh) & 1) * 16));
+    } else {
+      a_raw = x[A_OFF + vh];
+      b_raw = x[B_OFF + vh];
     }
     sq = warp_sum(sq);
     sk = warp_sum(sk);
@@ -339,6 +411,8 @@ __global__ void __launch_bounds__(PTHREADS, QC_GDN_CTAS) gdn_decode_persistent(c
       sm.red[PCONSUMERS + warp] = sk;
     }
     pconsumer_sync();
+    // every read of the prefetch buffer is done: fetch the next item's inputs
+    if (PRE && u + (int)gridDim.x < n_items) prefetch_item(sm, a, u + gridDim.x, tid);
     float tq = 0.0f, tk = 0.0f;
 #pragma unroll
     for (int w2 = 0; w2 < PCONSUMERS; ++w2) {
@@ -346,10 +420,10 @@ __global__ void __launch_bounds__(PTHREADS, QC_GDN_CTAS) gdn_decode_persistent(c
       tk += sm.red[PCONSUMERS + w2];
     }
     const float qs = 1.0f / sqrtf(tq + EPS), ks = 1.0f / sqrtf(tk + EPS);
-    const float biased = bf2f(x[A_OFF + vh]) + a.dt_bias[vh];
+    const float biased = bf2f(a_raw) + a.dt_bias[vh];
     const float sp = (biased > 20.0f) ? biased : logf(1.0f + expf(biased));
     const float decay = expf(sp * a.ssm_a[vh]);
-    const float beta = sigmoid_exact(bf2f(x[B_OFF + vh]));
+    const float beta = sigmoid_exact(bf2f(b_raw));
     float4 k4 = reinterpret_cast<const float4*>(sm.k)[lane];
     float4 q4 = reinterpret_cast<const float4*>(sm.q)[lane];
     k4.x *= ks; k4.y *= ks; k4.z *= ks; k4.w *= ks;
@@ -431,16 +505,27 @@ cudaError_t launch_persistent(const GdnArgs& a, cudaStream_t s) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(gdn_decode_persistent,
+    cudaError_t e = cudaFuncSetAttribute(gdn_decode_persistent<true>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)sizeof(PSmem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gdn_decode_persistent<false>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PSmem));
     if (e != cudaSuccess) return e;
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     configured_device = dev;
   }
   const int items = a.n * 32;
   const int grid = items < QC_GDN_CTAS * nsm ? items : QC_GDN_CTAS * nsm;
-  gdn_decode_persistent<<<grid, PTHREADS, sizeof(PSmem), s>>>(a);
+  // the prologue prefetch copies 16-byte runs: proj rows (24704 B apart),
+  // ring slots and conv weights must start on 16-byte boundaries
+  const bool aligned = ((reinterpret_cast<uintptr_t>(a.proj) | reinterpret_cast<uintptr_t>(a.ring) |
+                         reinterpret_cast<uintptr_t>(a.conv_w)) & 15) == 0 &&
+                       (a.ring_stride * 2) % 16 == 0;
+  if (aligned)
+    gdn_decode_persistent<true><<<grid, PTHREADS, sizeof(PSmem), s>>>(a);
+  else
+    gdn_decode_persistent<false><<<grid, PTHREADS, sizeof(PSmem), s>>>(a);
   return cudaGetLastError();
 }
 
