@@ -154,3 +154,40 @@ def test_golden_fixtures_on_gpu(qcache, synth, path_pat):
         np.testing.assert_array_equal(host_u16(kg)[L], g["k_new"])
         np.testing.assert_array_equal(host_u16(vg)[L], g["v_new"])
         q.close()
+
+
+@pytest.mark.parametrize("shape", ["ramp", "spike_first", "spike_last"])
+def test_softmax_reference_maximum_moves(qcache, synth, oracle, shape):
+    """Scores built so that the online softmax's reference maximum must move
+    by more than 2^8 from tile to tile (K rows of page t scaled by 1 + 3t,
+    scores up to ~250: every tile rescales), never moves after the first page
+    (the first page's keys scaled by 16), or moves only at the last page.
+    Kernel and oracle read the same bf16 cache."""
+    L = 1500
+    d = synth.attn_inputs(11, 1, L)
+    kf = synth.bf16_to_f32(d["k"][0]).copy()
+    p = np.arange(L)
+    if shape == "ramp":
+        kf *= (1.0 + 3.0 * (p // 64)).astype(np.float32)[:, None, None]
+    elif shape == "spike_first":
+        kf[:64] *= 16.0
+    else:
+        kf[-40:] *= 16.0
+    kb = synth.bf16_bits(kf)
+    q = make_ctx(qcache)
+    q.set_attn_params(0, d["q_norm"], d["k_norm"])
+    s = q.seq_alloc()
+    q.seq_reserve(s, L)
+    q.kv_write(s, 0, 0, L, dev(kb).data_ptr(), dev(d["v"][0]).data_ptr())
+    proj = dev(d["proj"])
+    out = empty_u16(1, 4096)
+    q.decode_begin([s])
+    q.attn_decode(0, proj.data_ptr(), out.data_ptr())
+    q.decode_end()
+    q.check_device()
+    kc = np.zeros((L + 1, 4, 256), np.uint16)
+    vc = np.zeros((L + 1, 4, 256), np.uint16)
+    kc[:L], vc[:L] = kb, d["v"][0]
+    ref = oracle_step(oracle, d, 0, L, kc, vc)
+    assert np.all(np.isfinite(ref))
+    assert_out_close(host_u16(out)[0], ref, synth)
