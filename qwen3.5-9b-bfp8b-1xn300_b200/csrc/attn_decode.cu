@@ -6,9 +6,11 @@
 // 32 KiB of V) in (sequence, kv-head, page) order — a split-K over KV
 // positions that balances the work exactly whatever the mix of context
 // lengths.  Warp 8 is the producer: it streams each page-head into a 3-stage
-// shared-memory ring with tiled TMA loads (cp.async.bulk.tensor, 16-row x
-// 128-byte boxes, 128-byte swizzle so that the ldmatrix reads below are free
-// of bank conflicts; each CTA loads only for itself).  Warps 0-7 are consumers; each takes 8 of
+// shared-memory ring with tiled TMA loads (cp.async.bulk.tensor, 64-row x
+// 128-byte boxes: 8 copies per 64 KiB page-head; 128-byte swizzle so that
+// the ldmatrix reads below are free of bank conflicts; each CTA loads only
+// for itself).  A partial last page is loaded whole; its rows past the
+// cached length are never read.  Warps 0-7 are consumers; each takes 8 of
 // the 64 positions of a tile for the 4 query heads of the GQA group
 // (kv_h = h / 4, src/engine.cpp:3532) and keeps its own online-softmax state.
 //
@@ -48,7 +50,7 @@ constexpr int STAGES = QC_ATTN_STAGES;
 constexpr int N_CONSUMER = 8;
 constexpr int THREADS = (N_CONSUMER + 1) * 32;
 constexpr int TILE_ELEMS = PAGE * HD;     // one K or V page-head, 32 KiB
-constexpr int BOX_ROWS = 16;              // TMA box: 16 rows x 64 bf16 (2 KiB)
+constexpr int BOX_ROWS = KV_BOX_ROWS;     // TMA box: rows x 64 bf16 (128 B per row)
 constexpr int BOX_BYTES = BOX_ROWS * 128;
 // score * 1/16 (src/model_config.h:40), kept in the log2 domain for exp2
 constexpr float SCALE_LOG2 = 0.0625f * 1.4426950408889634f;

@@ -139,7 +139,7 @@ extern "C" int qc_attn_decode_noalloc(const uint16_t* proj_dev, uint16_t* k_pool
   const cuuint64_t dims[2] = {(cuuint64_t)QC_HEAD_DIM,
                               (cuuint64_t)max_pages * QC_N_HEAD_KV * QC_PAGE};
   const cuuint64_t strides[1] = {(cuuint64_t)QC_HEAD_DIM * 2};
-  const cuuint32_t box[2] = {64, 16};
+  const cuuint32_t box[2] = {64, (cuuint32_t)qc::KV_BOX_ROWS};
   const cuuint32_t estr[2] = {1, 1};
   for (int kv = 0; kv < 2; ++kv) {
     CUresult r = g_encode(kv ? &tmv : &tmk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,

@@ -19,6 +19,10 @@ struct TraceRange {
   TraceRange& operator=(const TraceRange&) = delete;
 };
 
+// Rows of one TMA box of the K/V tensor maps (x 64 bf16 = 128 B, 128-byte
+// swizzle); the decode and prefill tile loads and the map encoders agree on it.
+constexpr int KV_BOX_ROWS = 64;
+
 
 // Gated-DeltaNet decode step (gdn_decode.cu).
 struct GdnArgs {

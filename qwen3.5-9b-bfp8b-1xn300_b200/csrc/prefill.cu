@@ -46,7 +46,7 @@ constexpr int HD = 256;
 constexpr int PAGE = 64;
 constexpr int ROWS = 4 * TMAX;                // query rows per kv-head: 4 heads x 32 tokens
 constexpr int PSTAGES = 2;
-constexpr int BOX_ROWS = 16;
+constexpr int BOX_ROWS = KV_BOX_ROWS;
 constexpr int BOX_BYTES = BOX_ROWS * 128;
 constexpr float SCALE_LOG2 = 0.0625f * 1.4426950408889634f;
 constexpr int REC = HD + 4;                   // record: m, l, 2 pad, o[256] (16 B aligned)

@@ -408,7 +408,7 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
       return cuda_fail(e, "rope upload");
   }
   // TMA tensor maps over each layer's K and V pool: [rows][256] bf16 with
-  // rows = max_pages * 4 kv-heads * 64 positions, 16 x 64 boxes, 128 B swizzle
+  // rows = max_pages * 4 kv-heads * 64 positions, KV_BOX_ROWS x 64 boxes, 128 B swizzle
   {
     PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     cudaDriverEntryPointQueryResult qres;
@@ -419,7 +419,7 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
     c->tm_v.resize(na);
     const cuuint64_t dims[2] = {(cuuint64_t)HD, (cuuint64_t)cfg->max_pages * QC_N_HEAD_KV * PAGE};
     const cuuint64_t strides[1] = {(cuuint64_t)HD * 2};
-    const cuuint32_t box[2] = {64, 16};
+    const cuuint32_t box[2] = {64, (cuuint32_t)qc::KV_BOX_ROWS};
     const cuuint32_t estr[2] = {1, 1};
     for (int l = 0; l < na; ++l)
       for (int kv = 0; kv < 2; ++kv) {
