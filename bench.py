@@ -48,7 +48,7 @@ GDN_BYTES_PER_LAUNCH = 4 * 8192 * 4 + 32 * 4 * 2 + 128 * 4   # conv weights + sm
 # the dominant kernel, per sequence, from the ncu captures summarised in
 # profiles/ (captured on smaller cases, scaled by the sequences processed):
 PROFILED_TRAFFIC_PER_SEQ = {
-    "stack": ("attn", (269.878784e6 + 4.500992e6) / 16,
+    "stack": ("attn", (273.006592e6 + 4.397824e6) / 16,
               "profiles/attn_partial_stack16.md (16 sequences, scaled)"),
     "long": ("attn", 537.116672e6 + 5.645312e6, "profiles/attn_partial_long131072.md"),
     "gdn": ("gdn", (139.216640e6 + 77.228800e6) / 64,
