@@ -1,7 +1,7 @@
-"""Benchmark of the per-token cache path (BASELINE metric: decode cache-path
+"""Benchmark of the per-token cache path (headline metric: decode cache-path
 µs/token/layer and HBM GB/s against 8 TB/s).
 
-Default workload (config 2 of the baseline): the full 32-layer hybrid cache
+Default workload (config 2 of the benchmark configurations): the full 32-layer hybrid cache
 stack (24 Gated-DeltaNet + 8 full-attention layers, attention at every 4th
 layer), 64 sequences at context 4096 in a paged bf16 KV cache (64-token pages,
 seeded random physical page order), one decode token per sequence per step,

@@ -26,7 +26,7 @@
 //   - decoded value = (-1)^sign * magnitude * 2^(shared_exp - 133).
 // Parity of the PACKER is unpinned against tt-metalium (no golden tiles ship
 // with the reference).  The decode rule is the format's definition, and the
-// GPU kernels are judged against this file's decode + fp32 dot products.
+// GPU kernels are checked against this file's decode + fp32 dot products.
 //
 // GEMV semantics (src/engine.cpp:371-486 dispatch_gemv, :498 dispatch_gemv_resadd,
 // :619 dispatch_gemv_split): y[b][m] = sum_k W[m][k] * x[b][k], x bf16,

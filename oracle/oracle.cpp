@@ -14,7 +14,7 @@
 // outputs.
 //
 // Math modes:
-//   QO_EXACT      libm expf/logf/sqrtf everywhere.  The GPU kernels are judged
+//   QO_EXACT      libm expf/logf/sqrtf everywhere.  The GPU kernels are checked
 //                 against this mode.
 //   QO_REF_APPROX Schraudolph exp in softplus, the beta / attention-gate
 //                 sigmoids and every SiLU, as the reference does
