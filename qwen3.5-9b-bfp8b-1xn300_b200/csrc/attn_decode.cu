@@ -676,15 +676,15 @@ int attn_smem_bytes() { return static_cast<int>(sizeof(Smem)) + 1024; }
 cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CUtensorMap& tmk,
                                const CUtensorMap& tmv, cudaStream_t s) {
   if (a.n <= 0) return cudaSuccess;
-  static int configured_device = -1;
+  static PerDeviceOnce configured;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (configured_device != dev) {
+  if (!configured.done(dev)) {
     cudaError_t e = cudaFuncSetAttribute(attn_partial_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          attn_smem_bytes());
     if (e != cudaSuccess) return e;
-    configured_device = dev;
+    configured.mark(dev);
   }
   attn_partial_kernel<<<a.grid, THREADS, attn_smem_bytes(), s>>>(a, tmk, tmv);
   cudaError_t e = cudaGetLastError();

@@ -500,11 +500,11 @@ __global__ void __launch_bounds__(PTHREADS, QC_GDN_CTAS) gdn_decode_persistent(c
 }
 
 cudaError_t launch_persistent(const GdnArgs& a, cudaStream_t s) {
-  static int configured_device = -1;
-  static int nsm = 148;
-  int dev = 0;
+  static PerDeviceOnce configured;
+  int dev = 0, nsm = 148;
   cudaGetDevice(&dev);
-  if (configured_device != dev) {
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  if (!configured.done(dev)) {
     cudaError_t e = cudaFuncSetAttribute(gdn_decode_persistent<true>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)sizeof(PSmem));
@@ -512,8 +512,7 @@ cudaError_t launch_persistent(const GdnArgs& a, cudaStream_t s) {
       e = cudaFuncSetAttribute(gdn_decode_persistent<false>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PSmem));
     if (e != cudaSuccess) return e;
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    configured_device = dev;
+    configured.mark(dev);
   }
   const int items = a.n * 32;
   const int grid = items < QC_GDN_CTAS * nsm ? items : QC_GDN_CTAS * nsm;
@@ -532,14 +531,14 @@ cudaError_t launch_persistent(const GdnArgs& a, cudaStream_t s) {
 template <int R, int T>
 cudaError_t launch_r(const GdnArgs& a, cudaStream_t s) {
   constexpr int smem = (HK / R) * HK * 4;
-  static int configured_device = -1;
+  static PerDeviceOnce configured;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (configured_device != dev) {
+  if (!configured.done(dev)) {
     cudaError_t e = cudaFuncSetAttribute(gdn_decode_kernel<R, T>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    configured_device = dev;
+    configured.mark(dev);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(32 * R, a.n, 1);

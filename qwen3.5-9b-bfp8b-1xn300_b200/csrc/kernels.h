@@ -2,6 +2,7 @@
 // device kernels.  Plain structs of device pointers and sizes.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -17,6 +18,23 @@ struct TraceRange {
   ~TraceRange() { nvtxRangePop(); }
   TraceRange(const TraceRange&) = delete;
   TraceRange& operator=(const TraceRange&) = delete;
+};
+
+// Which devices (ordinals below 64) have run a one-time setup, such as raising
+// a kernel's dynamic shared-memory limit.  Safe to query from the host threads
+// of several contexts at once; a device at or above 64 always reports "not
+// done", so its setup simply repeats.
+class PerDeviceOnce {
+ public:
+  bool done(int dev) const {
+    return dev >= 0 && dev < 64 && ((bits_.load(std::memory_order_acquire) >> dev) & 1u);
+  }
+  void mark(int dev) {
+    if (dev >= 0 && dev < 64) bits_.fetch_or(uint64_t(1) << dev, std::memory_order_release);
+  }
+
+ private:
+  std::atomic<uint64_t> bits_{0};
 };
 
 // Rows of one TMA box of the K/V tensor maps (x 64 bf16 = 128 B, 128-byte

@@ -163,12 +163,12 @@ cudaError_t launch_copy_jobs(const CopyJob* jobs_dev, int32_t n_jobs, const int6
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   const size_t smem = (size_t)BULK_STAGES * chunk;
-  static int configured_device = -1;
-  if (configured_device != dev) {
+  static PerDeviceOnce configured;
+  if (!configured.done(dev)) {
     cudaError_t e = cudaFuncSetAttribute(copy_jobs_bulk_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    configured_device = dev;
+    configured.mark(dev);
   }
   const int64_t grid = std::min<int64_t>(n_chunks, (int64_t)nsm * QC_BULK_CTAS);
   copy_jobs_bulk_kernel<<<static_cast<unsigned>(grid), 32, smem, s>>>(

@@ -654,15 +654,15 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(const AttnPrefillA
 
 cudaError_t launch_gdn_prefill(const GdnPrefillArgs& a, cudaStream_t s) {
   if (a.T <= 0) return cudaSuccess;
-  static int configured_device = -1;
+  static PerDeviceOnce configured;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (configured_device != dev) {
+  if (!configured.done(dev)) {
     cudaError_t e = cudaFuncSetAttribute(gdn_prefill_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)sizeof(GdnPrefillSmem));
     if (e != cudaSuccess) return e;
-    configured_device = dev;
+    configured.mark(dev);
   }
   gdn_prefill_conv_kernel<<<CONV / CONV_CH, 32 * (TMAX / CONV_TG), 0, s>>>(a);
   cudaError_t e0 = cudaGetLastError();
@@ -691,15 +691,15 @@ int attn_prefill_smem_bytes() { return (int)sizeof(TcSmem) + 1024; }
 cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, const CUtensorMap& tmk,
                                 const CUtensorMap& tmv, cudaStream_t s) {
   if (a.T <= 0) return cudaSuccess;
-  static int configured_device = -1;
+  static PerDeviceOnce configured;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (configured_device != dev) {
+  if (!configured.done(dev)) {
     cudaError_t e = cudaFuncSetAttribute(attn_prefill_tc_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          attn_prefill_smem_bytes());
     if (e != cudaSuccess) return e;
-    configured_device = dev;
+    configured.mark(dev);
   }
   prefill_qk_kernel<<<a.T, 640, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();

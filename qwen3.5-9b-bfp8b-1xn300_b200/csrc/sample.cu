@@ -363,14 +363,14 @@ __global__ void __launch_bounds__(ST, 1) sample_kernel(const SampleArgs a) {
 size_t sample_smem_bytes() { return sizeof(SampleSmem); }
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t s) {
-  static thread_local int configured_device = -1;
+  static PerDeviceOnce configured;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (configured_device != dev) {
+  if (!configured.done(dev)) {
     cudaError_t e = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)sizeof(SampleSmem));
     if (e != cudaSuccess) return e;
-    configured_device = dev;
+    configured.mark(dev);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(SC * a.batch, 1, 1);
