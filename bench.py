@@ -996,9 +996,13 @@ def main():
         if rank != 0:
             return
         us, cores, sample, _, _ = cpu_baseline()
+        ref_config = dict(config, timing="host wall clock of the CPU restatement of the "
+                          "reference's decode math (oracle port, all host threads) over a "
+                          "bounded sample of the workload", sharding="rank 0 only, host cores")
         emit({"impl": "reference", "metric": metric, "value": round(us, 3), "unit": "us",
               "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-              "higher_is_better": False, "dtype": "f32", "data": "synthetic", "config": config,
+              "higher_is_better": False, "dtype": "f32", "data": "synthetic",
+              "config": ref_config,
               "cpu_baseline": {"value": round(us, 3), "unit": "us/token/layer", "cores": cores,
                                "kind": "port", "sample": sample},
               "e2e": {"value": round(us, 3), "unit": "us", "h2d_bytes_per_step": 0,
