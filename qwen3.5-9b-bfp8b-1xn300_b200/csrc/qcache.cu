@@ -674,6 +674,28 @@ int qc_decode_begin(qc_ctx* c, const int32_t* seq_ids, int32_t n, const int32_t*
     if (c->seqs[s].len >= c->cfg.max_ctx)
       return fail(c, QC_ERR_ARG, "sequence %d is full (max_ctx %d)", s, c->cfg.max_ctx);
   }
+  {
+    // pages this step takes (a fresh page at a page boundary, a private copy
+    // of a shared tail page), counted before anything changes so that an
+    // exhausted pool leaves every sequence as it was
+    std::unordered_map<int32_t, int32_t> refs;  // tail page -> sharers left
+    size_t need = 0;
+    for (int32_t i = 0; i < n; ++i) {
+      const Seq& q = c->seqs[seq_ids[i]];
+      const int32_t pi = q.len / PAGE;
+      if (pi == (int32_t)q.pages.size()) {
+        ++need;
+        continue;
+      }
+      auto it = refs.emplace(q.pages[pi], c->page_ref[q.pages[pi]]).first;
+      if (it->second > 1) {
+        ++need;
+        --it->second;
+      }
+    }
+    if (need > c->free_pages.size())
+      return fail(c, QC_ERR_OOM, "KV page pool exhausted (%d pages)", c->cfg.max_pages);
+  }
   for (int32_t i = 0; i < n; ++i) {
     Seq& q = c->seqs[seq_ids[i]];
     const int32_t pi = q.len / PAGE;
@@ -835,7 +857,14 @@ int qc_prefill_begin(qc_ctx* c, int32_t s, int32_t n, const int32_t* tokens, qc_
                 c->cfg.max_ctx);
   std::vector<CopyJob> cow;
   const int32_t first = q.len / PAGE, last = (q.len + n - 1) / PAGE;
-  if (first < (int32_t)q.pages.size() && c->page_ref[q.pages[first]] > 1) {  // shared tail
+  const bool shared_tail = first < (int32_t)q.pages.size() && c->page_ref[q.pages[first]] > 1;
+  // checked before anything changes: an exhausted pool leaves the sequence
+  // as it was
+  const size_t need = (shared_tail ? 1 : 0) +
+                      (size_t)std::max<int32_t>(0, last + 1 - (int32_t)q.pages.size());
+  if (need > c->free_pages.size())
+    return fail(c, QC_ERR_OOM, "KV page pool exhausted (%d pages)", c->cfg.max_pages);
+  if (shared_tail) {
     const int32_t p = page_alloc(c);
     if (p < 0) return fail(c, QC_ERR_OOM, "KV page pool exhausted (%d pages)", c->cfg.max_pages);
     if (!c->host_only) page_copy_jobs(c, q.pages[first], p, cow);

@@ -188,3 +188,49 @@ def test_prefill_bookkeeping(qcache):
     assert q.match_prefix(s, list(range(65)) + [7]) == 65
     with pytest.raises(qcache.QCacheError):
         q.prefill_begin(s, 33)                       # chunk limit
+
+
+
+def _two_boundary_sequences_one_free_page(qcache):
+    """u, v: 128 tokens each (the next token of each needs a fresh page); the
+    pool left with exactly one free page."""
+    q = host_ctx(qcache, max_pages=32)
+    u, v = q.seq_alloc(), q.seq_alloc()
+    q.seq_reserve(u, 128)
+    q.seq_reserve(v, 128)
+    w = q.seq_alloc()
+    q.seq_reserve(w, 27 * 64)                            # 32 - 2 - 2 - 27 = 1 free
+    return q, u, v
+
+
+def test_decode_oom_leaves_every_sequence_unchanged(qcache):
+    """Two pages needed, one free: the step fails before any sequence of the
+    batch takes a page, and the single page still serves a one-sequence step."""
+    q, u, v = _two_boundary_sequences_one_free_page(qcache)
+    before = (q.seq_pages(u), q.seq_pages(v))
+    with pytest.raises(qcache.QCacheError) as e:
+        q.decode_begin([u, v])
+    assert e.value.code == qcache.QC_ERR_OOM
+    assert (q.seq_pages(u), q.seq_pages(v)) == before
+    q.decode_begin([v])
+    q.decode_end()
+    assert len(q.seq_pages(v)) == 3 and q.seq_pages(u) == before[0]
+
+
+def test_prefill_oom_leaves_sequence_unchanged(qcache):
+    """A chunk that crosses into two new pages with one free fails and leaves
+    the sequence's pages as they were; a chunk inside one new page fits."""
+    q, u, _ = _two_boundary_sequences_one_free_page(qcache)
+    before = q.seq_pages(u)
+    q.prefill_begin(u, 32)                               # positions 128..159: one page
+    q.prefill_end()
+    assert len(q.seq_pages(u)) == 3
+    q2, u2, _ = _two_boundary_sequences_one_free_page(qcache)
+    q2.seq_reserve(u2, 160)                              # takes the free page
+    before = q2.seq_pages(u2)
+    with pytest.raises(qcache.QCacheError) as e:
+        q2.prefill_begin(u2, 32)                         # 160..191 fits; 192 would not
+        q2.prefill_end()
+        q2.prefill_begin(u2, 1)
+    assert e.value.code == qcache.QC_ERR_OOM
+    assert q2.seq_pages(u2) == before
