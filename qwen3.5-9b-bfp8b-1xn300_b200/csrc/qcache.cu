@@ -1045,7 +1045,11 @@ int qc_prefix_insert(qc_ctx* c, int32_t s, const int32_t* tokens, int32_t n, int
     }
     if (tail >= 0) page_copy_jobs(c, q.pages[full], tail, jobs);
     int rc = run_jobs(c, jobs, (cudaStream_t)stream, nullptr);
-    if (rc) return rc;
+    if (rc) {  // give back what the entry took: page references, tail, slot
+      for (int32_t p : e.pages) page_decref(c, p);
+      c->free_snaps.push_back(e.snap);
+      return rc;
+    }
   }
   int32_t id = -1;
   for (int32_t i = 0; i < (int32_t)c->entries.size(); ++i)

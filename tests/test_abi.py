@@ -234,3 +234,26 @@ def test_prefill_oom_leaves_sequence_unchanged(qcache):
         q2.prefill_begin(u2, 1)
     assert e.value.code == qcache.QC_ERR_OOM
     assert q2.seq_pages(u2) == before
+
+
+def test_snapshot_slots_exhaust_and_return(qcache):
+    """Every entry holds one DeltaNet/conv snapshot slot: inserts beyond
+    max_snapshots fail with QC_ERR_OOM until an entry is released; releasing
+    every entry returns every page reference."""
+    q = host_ctx(qcache, max_pages=32, max_snapshots=2)
+    seqs = [q.seq_alloc() for _ in range(3)]
+    for i, s in enumerate(seqs):
+        q.seq_reserve(s, 70 + i)                         # one full page + a tail
+    e0 = q.prefix_insert(seqs[0], list(range(70)))
+    e1 = q.prefix_insert(seqs[1], list(range(100, 171)))
+    with pytest.raises(qcache.QCacheError) as e:
+        q.prefix_insert(seqs[2], list(range(200, 272)))
+    assert e.value.code == qcache.QC_ERR_OOM
+    q.prefix_release(e0)
+    e2 = q.prefix_insert(seqs[2], list(range(200, 272)))
+    for ent in (e1, e2):
+        q.prefix_release(ent)
+    for s in seqs:
+        q.seq_free(s)
+    u = q.seq_alloc()
+    q.seq_reserve(u, 32 * 64)                            # every page is free again
