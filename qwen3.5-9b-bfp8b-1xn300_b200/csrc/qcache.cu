@@ -1145,7 +1145,17 @@ int qc_prefix_restore(qc_ctx* c, const int32_t* entries, const int32_t* seqs, in
   if (!c->host_only) {
     cudaStream_t st = (cudaStream_t)stream;
     int rc = run_jobs(c, jobs, st, &c->last_restore_bytes);
-    if (rc) return rc;
+    if (rc) {  // the copies never ran: the sequences go back to empty
+      for (int32_t i = 0; i < n; ++i) {
+        Seq& q = c->seqs[seqs[i]];
+        for (int32_t p : q.pages) page_decref(c, p);
+        q.pages.clear();
+        q.len = 0;
+        q.tokens.clear();
+        set_row(c, seqs[i]);
+      }
+      return rc;
+    }
     if ((rc = sync_rows(c, st))) return rc;
     // the page-table rows are part of the restore traffic
     c->last_restore_bytes += 2LL * n * c->pt_stride * 4;
