@@ -1294,11 +1294,14 @@ int qc_p2p_create(qc_ctx* c, int32_t world, int32_t rank, void* handle_out) {
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, mbox_bytes(c, world));
   if (e != cudaSuccess) return fail(c, QC_ERR_OOM, "qc_p2p_create: %s", cudaGetErrorString(e));
-  c->mbox = static_cast<char*>(p);
-  QC_CUDA(c, cudaMemset(c->mbox, 0, mbox_bytes(c, world)));
-  QC_CUDA(c, cudaDeviceSynchronize());
   cudaIpcMemHandle_t h;
-  QC_CUDA(c, cudaIpcGetMemHandle(&h, c->mbox));
+  if ((e = cudaMemset(p, 0, mbox_bytes(c, world))) != cudaSuccess ||
+      (e = cudaDeviceSynchronize()) != cudaSuccess ||
+      (e = cudaIpcGetMemHandle(&h, p)) != cudaSuccess) {
+    cudaFree(p);  // nothing half-made stays behind: the call may be retried
+    return fail(c, QC_ERR_CUDA, "qc_p2p_create: %s", cudaGetErrorString(e));
+  }
+  c->mbox = static_cast<char*>(p);
   std::memcpy(handle_out, &h, sizeof(h));
   c->p2p_world = world;
   c->p2p_rank = rank;
