@@ -826,6 +826,16 @@ def gemv_cpu_baseline(budget_s=10.0, threads=None):
 # ------------------------------------------------------------ CPU baseline
 
 
+def oracle_build() -> str:
+    """Which build of the timed CPU restatement this host runs."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    name = oracle.fast_build_name()
+    isa = "x86-64-v4, AVX-512" if "512" in name else "x86-64-v3, AVX2"
+    return f"{name} (-O3 -ffast-math, {isa})"
+
+
 def cpu_baseline(budget_s: float = 12.0, threads: int | None = None):
     """The oracle's threaded C++ restatement of the reference's host math
     (liboracle_fast.so: the reference's -O3 -ffast-math), timed on this host
@@ -975,7 +985,7 @@ def main():
         if not args.no_cpu_baseline:
             cus, cores, sample = gemv_cpu_baseline()
             line["cpu_baseline"] = {"value": round(cus, 1), "unit": "us/decode step",
-                                    "cores": cores, "kind": "port", "sample": sample}
+                                    "cores": cores, "kind": "port", "sample": sample, "build": oracle_build()}
         emit(line)
         return
     if args.config in ("prefix", "prefill", "gemv"):
@@ -1004,7 +1014,7 @@ def main():
               "higher_is_better": False, "dtype": "f32", "data": "synthetic",
               "config": ref_config,
               "cpu_baseline": {"value": round(us, 3), "unit": "us/token/layer", "cores": cores,
-                               "kind": "port", "sample": sample},
+                               "kind": "port", "sample": sample, "build": oracle_build()},
               "e2e": {"value": round(us, 3), "unit": "us", "h2d_bytes_per_step": 0,
                       "d2h_bytes_per_step": 0}})
         return
@@ -1073,11 +1083,11 @@ def main():
     if not args.no_cpu_baseline and world == 1:
         cus, cores, sample, _, _ = cpu_baseline()
         line["cpu_baseline"] = {"value": round(cus, 3), "unit": "us/token/layer", "cores": cores,
-                                "kind": "port", "sample": sample}
+                                "kind": "port", "sample": sample, "build": oracle_build()}
         # the reference's own thread count: its WorkerPool (src/engine.cpp:1631)
         cus4, _, sample4, _, _ = cpu_baseline(budget_s=6.0, threads=4)
         line["cpu_baseline_4_threads"] = {"value": round(cus4, 3), "unit": "us/token/layer",
-                                          "cores": 4, "kind": "port", "sample": sample4}
+                                          "cores": 4, "kind": "port", "sample": sample4, "build": oracle_build()}
     emit(line)
     if dist is not None:
         dist.destroy_process_group()

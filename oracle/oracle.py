@@ -23,8 +23,24 @@ def build():
     subprocess.run(["make", "-s", "-C", HERE], check=True)
 
 
+def host_has_avx512() -> bool:
+    """True when the host CPU reports every x86-64-v4 feature (AVX-512 F, BW,
+    CD, DQ, VL), so the AVX-512 build of the timed baseline may run."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            flags = next((ln.split(":", 1)[1].split() for ln in f if ln.startswith("flags")), [])
+    except OSError:
+        return False
+    return {"avx512f", "avx512bw", "avx512cd", "avx512dq", "avx512vl"} <= set(flags)
+
+
+def fast_build_name() -> str:
+    """The timed-baseline build this host runs: AVX-512 when it can."""
+    return "liboracle_fast512.so" if host_has_avx512() else "liboracle_fast.so"
+
+
 def lib(fast: bool = False) -> C.CDLL:
-    name = "liboracle_fast.so" if fast else "liboracle.so"
+    name = fast_build_name() if fast else "liboracle.so"
     if name in _libs:
         return _libs[name]
     path = os.path.join(HERE, name)
