@@ -935,7 +935,7 @@ def main():
               "restore_ms_per_64": round(r["restore_ms"] / (r["n"] // 64), 4),
               "lookup_us_per_request": round(r["lookup_us"], 2),
               "decode_after_restore_us_token_layer": round(r["decode_us_token_layer"], 4),
-              "roofline": {"kernel": "copy_jobs_kernel (restore)", "bound": "hbm",
+              "roofline": {"kernel": "copy_jobs_bulk_kernel (restore)", "bound": "hbm",
                            "achieved": round(r["restore_gbs"], 1), "peak": peak,
                            "peak_kind": peak_kind, "unit": "GB/s",
                            "frac": round(r["restore_gbs"] / peak, 4), "traffic": None}})
