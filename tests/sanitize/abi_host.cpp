@@ -104,6 +104,34 @@ int main() {
   EXPECT(qc_prefix_release(q, e) == QC_OK);
   EXPECT(qc_prefix_release(q, 1234) != QC_OK);
 
+  {  // an exhausted pool or snapshot table leaves every sequence as it was
+    qc_config small = {8, 24, 4, 7, 4096, 4, 1, 0};
+    qc_ctx* r = nullptr;
+    EXPECT(qc_create(&small, QC_DEVICE_NONE, &r) == QC_OK && r);
+    int32_t u = -1, v = -1, w = -1;
+    EXPECT(qc_seq_alloc(r, &u) == QC_OK && qc_seq_alloc(r, &v) == QC_OK &&
+           qc_seq_alloc(r, &w) == QC_OK);
+    EXPECT(qc_seq_reserve(r, u, 128) == QC_OK && qc_seq_reserve(r, v, 128) == QC_OK);
+    EXPECT(qc_seq_reserve(r, w, 2 * 64) == QC_OK);          // 7 - 6 = 1 page free
+    const std::vector<int32_t> pu = pages(r, u), pv = pages(r, v);
+    int32_t both[2] = {u, v};
+    EXPECT(qc_decode_begin(r, both, 2, nullptr, nullptr) == QC_ERR_OOM);
+    EXPECT(pages(r, u) == pu && pages(r, v) == pv);
+    step(r, v, 5);                                           // one page: fits
+    EXPECT(pages(r, v).size() == 3 && pages(r, u) == pu);
+    std::vector<int32_t> toks(129);
+    for (int32_t i = 0; i < 129; ++i) toks[i] = i;
+    int32_t e1 = -1, e2 = -1;
+    EXPECT(qc_prefix_insert(r, u, toks.data(), 128, &e1, nullptr) == QC_OK);
+    EXPECT(qc_prefix_insert(r, v, toks.data(), 129, &e2, nullptr) == QC_ERR_OOM);  // no slot
+    EXPECT(qc_prefix_release(r, e1) == QC_OK);
+    // a slot again, but the entry's tail page cannot be had: nothing is taken
+    EXPECT(qc_prefix_insert(r, v, toks.data(), 129, &e2, nullptr) == QC_ERR_OOM);
+    EXPECT(qc_prefix_insert(r, u, toks.data(), 128, &e1, nullptr) == QC_OK);
+    EXPECT(qc_prefix_release(r, e1) == QC_OK);
+    qc_destroy(r);
+  }
+
   // peer-memory split-K needs a device; bad ranks are rejected first
   char handle[QC_P2P_HANDLE_BYTES];
   EXPECT(qc_p2p_create(q, 2, 0, handle) == QC_ERR_NODEVICE);
