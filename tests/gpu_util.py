@@ -35,16 +35,42 @@ def empty_u16(*shape) -> torch.Tensor:
     return torch.zeros(*shape, dtype=torch.int16, device="cuda")
 
 
+def out_errors(got_f32: np.ndarray, ref_f32: np.ndarray):
+    """(max |got - ref|, max |got - ref| / |ref| over elements with |ref| > OUT_ATOL)."""
+    err = np.abs(got_f32 - ref_f32)
+    big = np.abs(ref_f32) > OUT_ATOL
+    rel = float((err[big] / np.abs(ref_f32[big])).max()) if big.any() else 0.0
+    return float(err.max()) if err.size else 0.0, rel
+
+
 def assert_out_close(got_bits: np.ndarray, ref_f32: np.ndarray, synth):
+    """The output gate, two separate bounds: max-abs <= 2e-2 over every element
+    AND relative error <= 1e-2 on every element whose |ref| exceeds 2e-2 (below
+    that the bf16 rounding of a tiny value is governed by the absolute bound)."""
     got = synth.bf16_to_f32(got_bits).reshape(ref_f32.shape)
-    np.testing.assert_allclose(got, ref_f32, atol=OUT_ATOL, rtol=OUT_RTOL)
+    assert_f32_close(got, ref_f32)
+
+
+def assert_f32_close(got: np.ndarray, ref_f32: np.ndarray):
+    """assert_out_close on already-widened values."""
+    got = np.asarray(got, np.float32).reshape(ref_f32.shape)
+    assert np.all(np.isfinite(got)), "non-finite output"
+    mabs, mrel = out_errors(got, ref_f32)
+    assert mabs <= OUT_ATOL, f"max-abs {mabs:.3e} > {OUT_ATOL}"
+    assert mrel <= OUT_RTOL, f"max-rel {mrel:.3e} > {OUT_RTOL}"
 
 
 def assert_state_close(got: np.ndarray, ref: np.ndarray):
-    scale = np.abs(ref).max()
+    """The fp32 state, per element: |got - ref| <= 1e-4 * |ref| + 1e-6 * max|ref|.
+    The small absolute floor only covers elements that cancel to near zero
+    (their relative error is meaningless); every other element is held to
+    1e-4 relative."""
+    scale = float(np.abs(ref).max())
     err = np.abs(got - ref)
-    assert err.max() <= STATE_RTOL * scale, (err.max(), scale)
-    np.testing.assert_allclose(got, ref, rtol=STATE_RTOL, atol=STATE_RTOL * 1e-2 * scale)
+    bound = STATE_RTOL * np.abs(ref) + STATE_RTOL * 1e-2 * scale
+    bad = err > bound
+    assert not bad.any(), (f"{int(bad.sum())} state elements outside 1e-4 rel; worst "
+                           f"{float((err - bound).max()):.3e} over bound")
 
 
 def permute_free_pages(q, n_pages: int, seed: int):
