@@ -88,8 +88,11 @@ typedef struct qc_config {
 int qc_create(const qc_config* cfg, int device, qc_ctx** out);
 void qc_destroy(qc_ctx* ctx);
 const char* qc_last_error(const qc_ctx* ctx);
-/* Reads and clears the device error word written by kernels (QC_ERR_TIMEOUT /
- * QC_ERR_BOUNDS); synchronises the given stream first. */
+/* Reads and clears the device error words written by kernels (QC_ERR_TIMEOUT /
+ * QC_ERR_BOUNDS); synchronises the given stream first.  There is one word per
+ * launch site (kernel kind x layer), so qc_last_error names the kernel and the
+ * layer that failed first, as the reference's hang breadcrumbs name the layer
+ * and operation of a stuck call (src/engine.cpp:99-101, 4182-4185). */
 int qc_check_device(qc_ctx* ctx, qc_stream stream);
 
 /* Per-layer small weights, host pointers, copied to the device.
@@ -257,13 +260,29 @@ int qc_attn_combine(qc_ctx* ctx, const float* partials_dev, int32_t n_parts,
  *     then merges them as qc_attn_combine does.
  * Every rank must run the same steps and layers (qc_attn_partial_range opens
  * a step).  Destroy the contexts only after all ranks have finished their
- * last step. */
+ * last step.
+ * Failure: when a rank's records do not arrive within 1 s (a rank that died,
+ * stalled or skipped a layer), the merge gives up, qc_check_device reports
+ * QC_ERR_TIMEOUT naming the layer, and the mailbox is poisoned: the ranks'
+ * step counts no longer agree, so every later qc_attn_combine_p2p on this
+ * rank writes no output and reports QC_ERR_TIMEOUT again, and after
+ * qc_check_device has seen the timeout, qc_attn_partial_p2p and
+ * qc_attn_combine_p2p return QC_ERR_ARG.  To recover, every surviving rank
+ * closes its step (qc_decode_abort), synchronises its stream, meets the
+ * others at a host barrier, calls qc_p2p_reset (zeroes its own counters, step
+ * counts and poison word), and meets them at a second barrier before the
+ * next step.  A rank that is gone must be replaced, or the mailboxes
+ * recreated with the new world size.
+ */
 #define QC_P2P_HANDLE_BYTES 64
 int qc_p2p_create(qc_ctx* ctx, int32_t world, int32_t rank, void* handle_out);
 int qc_p2p_open(qc_ctx* ctx, int32_t peer, const void* handle);
 int qc_attn_partial_p2p(qc_ctx* ctx, int attn_layer, const uint16_t* proj_dev, qc_stream stream);
 int qc_attn_combine_p2p(qc_ctx* ctx, int attn_layer, const uint16_t* proj_dev, uint16_t* out_dev,
                         qc_stream stream);
+/* Clears this rank's mailbox counters, step counts and poison word (see
+ * "Failure" above); synchronises the stream.  No decode step may be open. */
+int qc_p2p_reset(qc_ctx* ctx, qc_stream stream);
 
 /* ------------------------------------------- decode without device allocation */
 
@@ -285,8 +304,10 @@ int qc_attn_combine_p2p(qc_ctx* ctx, int attn_layer, const uint16_t* proj_dev, u
  * QC_NOALLOC_MAX_CTAS SMs; larger requests return QC_ERR_ARG.  All calls on a
  * device share that array: calls that overlap on the GPU race, so serialise
  * them.  The first call on each device looks up the array's address with that
- * device current; make it before any stream capture.  On failure
- * qc_last_error(NULL) describes the error. */
+ * device current; make it before any stream capture.  The step descriptor
+ * travels as a kernel parameter, so the call reads no host memory
+ * asynchronously and does not wait for earlier work on the stream.  On
+ * failure qc_last_error(NULL) describes the error. */
 #define QC_NOALLOC_MAX_BATCH 64
 #define QC_NOALLOC_MAX_CTAS  192
 int qc_attn_decode_noalloc(const uint16_t* proj_dev, uint16_t* k_pool_dev, uint16_t* v_pool_dev,
@@ -294,6 +315,12 @@ int qc_attn_decode_noalloc(const uint16_t* proj_dev, uint16_t* k_pool_dev, uint1
                            const int32_t* pos, int32_t n, const float* q_norm_dev,
                            const float* k_norm_dev, const float* rope_cos_dev,
                            const float* rope_sin_dev, uint16_t* out_dev, qc_stream stream);
+/* Errors the kernels of qc_attn_decode_noalloc found on the current device
+ * (a page-table entry outside [0, max_pages): QC_ERR_BOUNDS, that tile was
+ * skipped and the output is wrong; an expired wait: QC_ERR_TIMEOUT), collected
+ * over every call since the last check.  Synchronises the stream, returns the
+ * code (message in qc_last_error(NULL)) and clears it.  Allocates nothing. */
+int qc_attn_noalloc_check(qc_stream stream);
 
 #ifdef __cplusplus
 }

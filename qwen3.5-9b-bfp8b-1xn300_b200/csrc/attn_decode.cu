@@ -617,8 +617,18 @@ __global__ void __launch_bounds__(256) attn_merge_records_kernel(const float* re
 __global__ void __launch_bounds__(256) attn_merge_mailbox_kernel(const MailboxMergeArgs m) {
   __shared__ int ok;
   const int h = blockIdx.x, t = threadIdx.x;
+  if (t == 0) ok = 1;
   const uint32_t step = m.done[m.layer] + 1u;
   if (t == 0) {
+    // a merge that gave up earlier left the step counts of the ranks apart:
+    // every later merge refuses (no output) until qc_p2p_reset clears this
+    if (*reinterpret_cast<volatile uint32_t*>(m.poison)) {
+      record_error(m.err, QC_ERR_TIMEOUT);
+      ok = 0;
+    }
+  }
+  __syncthreads();
+  if (t == 0 && ok != 0) {
     const uint32_t target = 16u * step;
     const uint32_t* cnt = m.cnt + m.layer * m.world;
     const uint64_t t0 = globaltimer();
@@ -633,6 +643,7 @@ __global__ void __launch_bounds__(256) attn_merge_mailbox_kernel(const MailboxMe
       if (done) break;
       if ((it & 63u) == 0 && globaltimer() - t0 > WAIT_LIMIT_NS) {
         record_error(m.err, QC_ERR_TIMEOUT);
+        atomicExch(m.poison, 1u);
         break;
       }
     }

@@ -20,10 +20,17 @@
 //     host threads) race and give wrong results — serialise them;
 //   - the first call on each device looks up the array's device address
 //     (cudaGetSymbolAddress, with that device current); make that first call
-//     before any stream capture.
+//     before any stream capture;
+//   - the step descriptor reaches the device as a kernel parameter (a small
+//     kernel stores it into the array), so a call copies nothing from host
+//     memory and does not wait for earlier work on the stream;
+//   - the kernels' error word also lives in the array: it collects
+//     QC_ERR_BOUNDS / QC_ERR_TIMEOUT from every call on the device until
+//     qc_attn_noalloc_check reads and clears it.
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <cudaTypedefs.h>
 
 #include "../../include/qcache.h"
@@ -49,12 +56,24 @@ constexpr size_t SCRATCH_WORDS = E_OFF + 4;
 static __device__ __align__(256) float g_noalloc_scratch[SCRATCH_WORDS];
 
 struct DeviceSetup {
-  bool done = false;
+  std::once_flag once;
+  int rc = QC_OK;            // outcome of the one-time setup
+  char msg[160] = {};
   float* scratch = nullptr;  // device address of g_noalloc_scratch
   int nsm = 0;
 };
 DeviceSetup g_setup[MAX_DEVICES];
+std::once_flag g_encode_once;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+// The step descriptor, passed by value to the kernel that stores it.
+struct Desc {
+  int32_t w[DESC_WORDS];
+};
+
+__global__ void noalloc_store_desc_kernel(const Desc d, int32_t words, int32_t* dst) {
+  for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = d.w[i];
+}
 
 int err(int code, const char* fmt, ...) {
   char buf[256];
@@ -95,27 +114,33 @@ extern "C" int qc_attn_decode_noalloc(const uint16_t* proj_dev, uint16_t* k_pool
 
   // once per device, with that device current
   DeviceSetup& su = g_setup[dev];
-  if (!su.done) {
-    e = cudaGetSymbolAddress((void**)&su.scratch, g_noalloc_scratch);
-    if (e != cudaSuccess)
-      return err(QC_ERR_CUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    e = cudaDeviceGetAttribute(&su.nsm, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess)
-      return err(QC_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
-    if (!g_encode) {
-      cudaDriverEntryPointQueryResult qres;
-      e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", (void**)&g_encode, cudaEnableDefault,
-                                  &qres);
-      if (e != cudaSuccess || !g_encode || qres != cudaDriverEntryPointSuccess)
-        return err(QC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  std::call_once(su.once, [&su, dev] {
+    cudaError_t e2 = cudaGetSymbolAddress((void**)&su.scratch, g_noalloc_scratch);
+    if (e2 == cudaSuccess) e2 = cudaDeviceGetAttribute(&su.nsm, cudaDevAttrMultiProcessorCount, dev);
+    if (e2 != cudaSuccess) {
+      su.rc = QC_ERR_CUDA;
+      snprintf(su.msg, sizeof(su.msg), "qc_attn_decode_noalloc setup: %s", cudaGetErrorString(e2));
+      return;
     }
-    su.done = true;
-  }
+    std::call_once(g_encode_once, [] {
+      cudaDriverEntryPointQueryResult qres;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", (void**)&g_encode, cudaEnableDefault,
+                                  &qres) != cudaSuccess ||
+          qres != cudaDriverEntryPointSuccess)
+        g_encode = nullptr;
+    });
+    if (!g_encode) {
+      su.rc = QC_ERR_CUDA;
+      snprintf(su.msg, sizeof(su.msg), "cuTensorMapEncodeTiled unavailable");
+    }
+  });
+  if (su.rc != QC_OK) return err(su.rc, "%s", su.msg);
   if (su.nsm > MAX_CTAS)
     return err(QC_ERR_ARG, "qc_attn_decode_noalloc: %d SMs, limit is %d", su.nsm, MAX_CTAS);
 
   // descriptor: slots (= page-table rows 0..n-1) | pos | seg | page0 | append | total, per
-  int32_t d[DESC_WORDS];
+  Desc dd;
+  int32_t* d = dd.w;
   d[2 * n] = 0;
   for (int32_t i = 0; i < n; ++i) {
     d[i] = i;
@@ -130,9 +155,9 @@ extern "C" int qc_attn_decode_noalloc(const uint16_t* proj_dev, uint16_t* k_pool
   d[5 * n + 2] = per;
   int32_t* desc = reinterpret_cast<int32_t*>(su.scratch + D_OFF);
   cudaStream_t st = (cudaStream_t)stream;
-  // pageable source: the runtime copies it out before returning
-  e = cudaMemcpyAsync(desc, d, (size_t)(5 * n + 3) * 4, cudaMemcpyHostToDevice, st);
-  if (e != cudaSuccess) return err(QC_ERR_CUDA, "descriptor upload: %s", cudaGetErrorString(e));
+  noalloc_store_desc_kernel<<<1, 128, 0, st>>>(dd, 5 * n + 3, desc);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return err(QC_ERR_CUDA, "descriptor store: %s", cudaGetErrorString(e));
 
   // tensor maps over the caller's pools (host-side encoding, no allocation)
   CUtensorMap tmk, tmv;
@@ -184,5 +209,27 @@ extern "C" int qc_attn_decode_noalloc(const uint16_t* proj_dev, uint16_t* k_pool
   cb.n = n;
   e = qc::launch_attn_decode(a, cb, tmk, tmv, st);
   if (e != cudaSuccess) return err(QC_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
+  return QC_OK;
+}
+
+extern "C" int qc_attn_noalloc_check(qc_stream stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return err(QC_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= MAX_DEVICES) return err(QC_ERR_ARG, "device %d out of range", dev);
+  DeviceSetup& su = g_setup[dev];
+  // no call has run on this device yet (the setup records its outcome first)
+  if (!su.scratch) return su.rc != QC_OK ? err(su.rc, "%s", su.msg) : QC_OK;
+  e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return err(QC_ERR_CUDA, "stream: %s", cudaGetErrorString(e));
+  int* word = reinterpret_cast<int*>(su.scratch + E_OFF);
+  int code = 0;
+  e = cudaMemcpy(&code, word, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && code) e = cudaMemset(word, 0, sizeof(int));
+  if (e != cudaSuccess) return err(QC_ERR_CUDA, "error word: %s", cudaGetErrorString(e));
+  if (code)
+    return err(code, "qc_attn_decode_noalloc: the device reported %s",
+               code == QC_ERR_BOUNDS ? "a page id out of range (that tile was skipped)"
+               : code == QC_ERR_TIMEOUT ? "a wait timeout" : "an error");
   return QC_OK;
 }

@@ -37,8 +37,9 @@ class PerDeviceOnce {
   std::atomic<uint64_t> bits_{0};
 };
 
-// Rows of one TMA box of the K/V tensor maps (x 64 bf16 = 128 B, 128-byte
-// swizzle); the decode and prefill tile loads and the map encoders agree on it.
+// Rows of one TMA box of the K/V tensor maps (64 rows x 64 bf16 = 8 KiB,
+// 128-byte swizzle); the decode and prefill tile loads and the map encoders
+// agree on it.
 constexpr int KV_BOX_ROWS = 64;
 
 
@@ -110,7 +111,8 @@ struct CombineArgs {
   const uint32_t* done;                    // this rank's merged steps per layer
 };
 // tmk / tmv: 2D tensor maps over this layer's K / V pool viewed as
-// [max_pages * 4 * 64 rows][256 bf16], box 16 rows x 64 columns, 128 B swizzle.
+// [max_pages * 4 * 64 rows][256 bf16], box KV_BOX_ROWS rows x 64 columns,
+// 128 B swizzle.
 cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CUtensorMap& tmk,
                                const CUtensorMap& tmv, cudaStream_t s);
 int attn_smem_bytes();
@@ -126,6 +128,7 @@ struct MailboxMergeArgs {
   const uint32_t* cnt;     // this rank's counters [n_layers][world]
   uint32_t* done;          // [n_layers] steps merged
   uint32_t* consumed;      // [n_layers] CTAs finished, for advancing done
+  uint32_t* poison;        // set by a wait that gave up; later merges refuse until reset
   int32_t world, layer, n_layers;
   const uint16_t* proj;
   uint16_t* out;

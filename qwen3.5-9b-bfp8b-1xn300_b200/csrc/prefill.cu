@@ -469,9 +469,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         const int pid = a.page_row[pg];
         const int rows = min(PAGE, end - pg * PAGE);
-        // all 64 rows of a valid page: the P.V product reads every row of the
-        // tile (P is zero past `rows`), so none may be stale shared memory;
-        // pool rows are zeroed at creation or hold finite older tokens
+        // all 64 rows of a valid page (one box per 64 rows); the softmax
+        // warps zero the rows past `rows` before P.V reads them
         const int nbox = (pid >= 0 && pid < a.max_pages) ? PAGE / BOX_ROWS : 0;
         if (nbox == 0) record_error(a.err, QC_ERR_BOUNDS);
         (void)rows;
@@ -542,6 +541,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_before();
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (row == 0) mbar_arrive(&sm.s_free[b]);
+      // rows of the page past its valid length hold whatever an earlier
+      // sequence left in a reused page (possibly not finite): P is zero there,
+      // but 0 * Inf would still reach O, so zero those V rows before P.V reads
+      // them.  The tile landed (S(i) was computed from it); the proxy fence
+      // before p_full orders these stores before the tensor-core read.  A row
+      // is 128 B in each of the four 64-column boxes of the stage.
+      if (rows < PAGE) {
+        unsigned char* vs = reinterpret_cast<unsigned char*>(sm.v[i % PSTAGES]);
+        for (int k = row; k < (PAGE - rows) * 32; k += 128) {
+          const int r = rows + k / 32, cb = (k % 32) / 8, c16 = k % 8;
+          *reinterpret_cast<uint4*>(vs + cb * PAGE * 128 + r * 128 + c16 * 16) =
+              make_uint4(0, 0, 0, 0);
+        }
+      }
       // mask (position exists; causal inside the chunk) and scale
       float mt = -INFINITY;
 #pragma unroll

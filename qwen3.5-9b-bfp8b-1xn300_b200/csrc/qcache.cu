@@ -88,6 +88,7 @@ struct qc_ctx {
   int32_t p2p_world = 0, p2p_rank = -1;
   char* mbox = nullptr;         // this rank's mailbox (records, then counters)
   char* peer_mbox[QC_P2P_MAX_RANKS] = {};  // every rank's mailbox, self included
+  bool p2p_poisoned = false;    // a merge wait expired: refuse until qc_p2p_reset
   float* part_m = nullptr;
   float* part_l = nullptr;
   float* part_o = nullptr;
@@ -95,7 +96,8 @@ struct qc_ctx {
   CopyJob* jobs = nullptr;
   int64_t* chunk_start = nullptr;
   int32_t job_cap = 0;
-  int* dev_err = nullptr;
+  int* dev_err = nullptr;       // error words [EK_COUNT][err_layers], see err_site
+  int32_t err_layers = 1;
   uint16_t* pf_q = nullptr;     // prefill: q tile [4][128][256] bf16
   float* pf_rec = nullptr;      // prefill: records [4][pf_split][128][260] f32
   float* pf_conv = nullptr;     // prefill: conv outputs [32][8192] f32
@@ -130,6 +132,25 @@ struct qc_ctx {
 };
 
 namespace {
+
+// Device error words: one per launch site (kernel kind x layer).  A kernel
+// records QC_ERR_TIMEOUT / QC_ERR_BOUNDS into its site's word, so that
+// qc_check_device can say which kernel of which layer failed, as the
+// reference's hang breadcrumbs name the layer and operation of a stuck device
+// call (src/engine.cpp:99-101, 4182-4185).
+enum ErrKind {
+  EK_ATTN_DECODE, EK_ATTN_MERGE, EK_GDN_DECODE, EK_ATTN_PREFILL, EK_KV_COPY, EK_COPY_JOBS,
+  EK_COUNT
+};
+const char* const kErrKindName[EK_COUNT] = {
+    "attention decode (attn_partial_kernel)", "peer-record merge (attn_merge_mailbox_kernel)",
+    "DeltaNet decode (gdn_decode_kernel)", "attention prefill (attn_prefill_tc_kernel)",
+    "KV scatter/gather (kv_scatter_kernel / kv_gather_kernel)",
+    "batched copy (copy_jobs_bulk_kernel)"};
+
+int* err_site(qc_ctx* c, int kind, int layer) {
+  return c->dev_err + (int64_t)kind * c->err_layers + layer;
+}
 
 int fail(qc_ctx* c, int code, const char* fmt, ...) {
   char buf[512];
@@ -237,7 +258,7 @@ int run_jobs(qc_ctx* c, const std::vector<CopyJob>& jobs, cudaStream_t s, int64_
   int rc = stage_release(c, si, s);
   if (rc) return rc;
   QC_CUDA(c, qc::launch_copy_jobs(c->jobs, (int32_t)jobs.size(), c->chunk_start, starts.back(),
-                                  COPY_CHUNK, c->dev_err, s));
+                                  COPY_CHUNK, err_site(c, EK_COPY_JOBS, 0), s));
   if (bytes_out) *bytes_out += 2 * total;
   return QC_OK;
 }
@@ -346,6 +367,7 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
   c->part_slots = 4 * cfg->max_batch + c->nsm + 8;
   c->pf_split = (c->nsm + 3) / 4;
   c->job_cap = cfg->max_batch * (1 + 3 * std::max(ng, 1) + 2 * na) + 64;
+  c->err_layers = std::max({na, ng, 1});
   struct A { void** p; size_t bytes; const char* what; };
   const A allocs[] = {
       {(void**)&c->k_pool, (size_t)pool * 2, "k_pool"},
@@ -370,7 +392,7 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
       {(void**)&c->part_o, (size_t)c->part_slots * 4 * HD * 4, "part_o"},
       {(void**)&c->jobs, (size_t)c->job_cap * sizeof(CopyJob), "jobs"},
       {(void**)&c->chunk_start, (size_t)(c->job_cap + 1) * 8, "chunk_start"},
-      {(void**)&c->dev_err, 16, "dev_err"},
+      {(void**)&c->dev_err, (size_t)EK_COUNT * c->err_layers * 4, "dev_err"},
       {(void**)&c->pf_q, (size_t)4 * 4 * QC_PREFILL_CHUNK * HD * 2, "prefill q"},
       {(void**)&c->pf_conv, (size_t)QC_PREFILL_CHUNK * QC_CONV_CH * 4, "prefill conv"},
       {(void**)&c->pf_rec, (size_t)4 * c->pf_split * 4 * QC_PREFILL_CHUNK * (HD + 4) * 4,
@@ -389,7 +411,7 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
   if ((e = cudaMemset(c->state, 0, (size_t)cfg->max_seqs * std::max(ng, 1) * QC_GDN_STATE * 4)) ||
       (e = cudaMemset(c->ring, 0, (size_t)cfg->max_seqs * std::max(ng, 1) * RING_ELEMS * 2)) ||
       (e = cudaMemset(c->page_table, 0xff, (size_t)cfg->max_seqs * c->pt_stride * 4)) ||
-      (e = cudaMemset(c->dev_err, 0, 16)))
+      (e = cudaMemset(c->dev_err, 0, (size_t)EK_COUNT * c->err_layers * 4)))
     return cuda_fail(e, "cudaMemset");
 
   // RoPE table, the formula of precompute_rope (src/engine.cpp:2408-2420)
@@ -471,11 +493,29 @@ int qc_check_device(qc_ctx* c, qc_stream stream) {
   if (!c) return QC_ERR_ARG;
   QC_NEED_DEVICE(c);
   QC_CUDA(c, cudaStreamSynchronize((cudaStream_t)stream));
-  int code = 0;
-  QC_CUDA(c, cudaMemcpy(&code, c->dev_err, 4, cudaMemcpyDeviceToHost));
-  QC_CUDA(c, cudaMemset(c->dev_err, 0, 4));
-  if (code) return fail(c, code, "device reported error %d", code);
-  return QC_OK;
+  const size_t nw = (size_t)EK_COUNT * c->err_layers;
+  std::vector<int> words(nw);
+  QC_CUDA(c, cudaMemcpy(words.data(), c->dev_err, nw * 4, cudaMemcpyDeviceToHost));
+  int code = 0, sites = 0;
+  std::string where;
+  for (size_t i = 0; i < nw; ++i) {
+    if (!words[i]) continue;
+    if (!code) {
+      code = words[i];
+      char buf[256];
+      snprintf(buf, sizeof(buf), "%s, layer %d", kErrKindName[i / c->err_layers],
+               (int)(i % c->err_layers));
+      where = buf;
+    }
+    ++sites;
+  }
+  if (!code) return QC_OK;
+  QC_CUDA(c, cudaMemset(c->dev_err, 0, nw * 4));
+  for (int l = 0; l < c->err_layers; ++l)
+    if (words[(size_t)EK_ATTN_MERGE * c->err_layers + l] == QC_ERR_TIMEOUT) c->p2p_poisoned = true;
+  return fail(c, code, "device reported %s in %s%s", code == QC_ERR_TIMEOUT ? "a wait timeout"
+              : code == QC_ERR_BOUNDS ? "an index out of bounds" : "an error",
+              where.c_str(), sites > 1 ? " (and other launch sites)" : "");
 }
 
 int qc_set_attn_params(qc_ctx* c, int layer, const float* q_norm, const float* k_norm) {
@@ -608,7 +648,7 @@ int qc_kv_write(qc_ctx* c, int32_t s, int layer, int32_t pos0, int32_t n, const 
   const int64_t base = (int64_t)layer * c->cfg.max_pages * PAGE_ELEMS;
   QC_CUDA(c, qc::launch_kv_scatter(c->k_pool + base, c->v_pool + base,
                                    c->page_table + (int64_t)s * c->pt_stride, pos0, n, k, v,
-                                   c->cfg.max_pages, c->dev_err, st));
+                                   c->cfg.max_pages, err_site(c, EK_KV_COPY, layer), st));
   return QC_OK;
 }
 
@@ -623,7 +663,7 @@ int qc_kv_read(qc_ctx* c, int32_t s, int layer, int32_t pos0, int32_t n, uint16_
   const int64_t base = (int64_t)layer * c->cfg.max_pages * PAGE_ELEMS;
   QC_CUDA(c, qc::launch_kv_gather(c->k_pool + base, c->v_pool + base,
                                   c->page_table + (int64_t)s * c->pt_stride, pos0, n, k, v,
-                                  c->cfg.max_pages, c->dev_err, st));
+                                  c->cfg.max_pages, err_site(c, EK_KV_COPY, layer), st));
   return QC_OK;
 }
 
@@ -784,7 +824,7 @@ int qc_attn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc
   a.split = c->desc + 5 * n + 1;
   a.n = n;
   a.grid = c->b_grid;
-  a.err = c->dev_err;
+  a.err = err_site(c, EK_ATTN_DECODE, layer);
   qc::CombineArgs cb{};
   cb.proj = proj;
   cb.out = out;
@@ -819,7 +859,7 @@ int qc_gdn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc_
   g.slots = c->desc;
   g.pos = c->desc + n;
   g.n = n;
-  g.err = c->dev_err;
+  g.err = err_site(c, EK_GDN_DECODE, layer);
   QC_CUDA(c, qc::launch_gdn_decode(g, (cudaStream_t)stream));
   return QC_OK;
 }
@@ -925,7 +965,7 @@ int qc_attn_prefill(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, q
   // at least 4 pages per CTA: each CTA's fixed cost (tensor-memory setup, the
   // 64 KiB q tile, a 133 KB record) must be spread over several tiles
   a.n_split = std::max(1, std::min(c->pf_split, n_pages / 4));
-  a.err = c->dev_err;
+  a.err = err_site(c, EK_ATTN_PREFILL, layer);
   QC_CUDA(c, qc::launch_attn_prefill(a, c->tm_k[layer], c->tm_v[layer], (cudaStream_t)stream));
   return QC_OK;
 }
@@ -1250,7 +1290,7 @@ int qc_attn_partial(qc_ctx* c, int layer, const uint16_t* proj, float* partial,
   a.part_o = c->part_o;
   a.n = 1;
   a.grid = c->nsm;
-  a.err = c->dev_err;
+  a.err = err_site(c, EK_ATTN_DECODE, layer);
   qc::CombineArgs cb{};
   cb.proj = proj;
   cb.out = nullptr;
@@ -1281,8 +1321,11 @@ int qc_attn_combine(qc_ctx* c, const float* partials, int32_t n_parts, const uin
 static size_t mbox_rec_bytes(const qc_ctx* c, int world) {
   return (size_t)2 * c->cfg.n_attn_layers * world * 16 * 258 * sizeof(float);
 }
+// records, then counters [n_layers][world], done [n_layers], consumed
+// [n_layers], and one poison word (set by a merge whose wait expired)
 static size_t mbox_bytes(const qc_ctx* c, int world) {
-  return mbox_rec_bytes(c, world) + (size_t)c->cfg.n_attn_layers * (world + 2) * sizeof(uint32_t);
+  return mbox_rec_bytes(c, world) +
+         ((size_t)c->cfg.n_attn_layers * (world + 2) + 1) * sizeof(uint32_t);
 }
 
 int qc_p2p_create(qc_ctx* c, int32_t world, int32_t rank, void* handle_out) {
@@ -1325,6 +1368,26 @@ int qc_p2p_open(qc_ctx* c, int32_t peer, const void* handle) {
   return QC_OK;
 }
 
+static uint32_t* mbox_done(qc_ctx* c);
+
+int qc_p2p_reset(qc_ctx* c, qc_stream stream) {
+  qc::TraceRange trace_("qc_p2p_reset");
+  if (!c) return QC_ERR_ARG;
+  QC_NEED_DEVICE(c);
+  if (!c->mbox) return fail(c, QC_ERR_ARG, "qc_p2p_reset: no peer mailbox (qc_p2p_create)");
+  if (c->in_step) return fail(c, QC_ERR_ARG, "qc_p2p_reset: a decode step is open");
+  cudaSetDevice(c->device);
+  QC_CUDA(c, cudaStreamSynchronize((cudaStream_t)stream));
+  // counters, done, consumed and the poison word; the records need no
+  // clearing (a step's records are read only once its counters are complete)
+  const size_t off = mbox_rec_bytes(c, c->p2p_world);
+  QC_CUDA(c, cudaMemsetAsync(c->mbox + off, 0, mbox_bytes(c, c->p2p_world) - off,
+                             (cudaStream_t)stream));
+  QC_CUDA(c, cudaStreamSynchronize((cudaStream_t)stream));
+  c->p2p_poisoned = false;
+  return QC_OK;
+}
+
 static uint32_t* mbox_done(qc_ctx* c) {
   return reinterpret_cast<uint32_t*>(c->mbox + mbox_rec_bytes(c, c->p2p_world)) +
          (size_t)c->cfg.n_attn_layers * c->p2p_world;
@@ -1332,6 +1395,9 @@ static uint32_t* mbox_done(qc_ctx* c) {
 
 static int p2p_ready(qc_ctx* c) {
   if (!c->mbox) return fail(c, QC_ERR_ARG, "no peer mailbox (qc_p2p_create)");
+  if (c->p2p_poisoned)
+    return fail(c, QC_ERR_ARG, "a peer-record wait expired: the mailbox step counts are out of "
+                               "step until every rank has called qc_p2p_reset");
   for (int r = 0; r < c->p2p_world; ++r)
     if (!c->peer_mbox[r]) return fail(c, QC_ERR_ARG, "peer %d not opened (qc_p2p_open)", r);
   return QC_OK;
@@ -1370,7 +1436,7 @@ int qc_attn_partial_p2p(qc_ctx* c, int layer, const uint16_t* proj, qc_stream st
   a.part_o = c->part_o;
   a.n = 1;
   a.grid = c->nsm;
-  a.err = c->dev_err;
+  a.err = err_site(c, EK_ATTN_DECODE, layer);
   qc::CombineArgs cb{};
   cb.proj = proj;
   cb.seg = a.seg;
@@ -1405,12 +1471,13 @@ int qc_attn_combine_p2p(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* ou
   m.cnt = reinterpret_cast<const uint32_t*>(c->mbox + mbox_rec_bytes(c, c->p2p_world));
   m.done = mbox_done(c);
   m.consumed = mbox_done(c) + c->cfg.n_attn_layers;
+  m.poison = mbox_done(c) + 2 * c->cfg.n_attn_layers;
   m.world = c->p2p_world;
   m.layer = layer;
   m.n_layers = c->cfg.n_attn_layers;
   m.proj = proj;
   m.out = out;
-  m.err = c->dev_err;
+  m.err = err_site(c, EK_ATTN_MERGE, layer);
   QC_CUDA(c, qc::launch_attn_merge_mailbox(m, (cudaStream_t)stream));
   return QC_OK;
 }

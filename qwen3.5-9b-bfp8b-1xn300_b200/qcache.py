@@ -110,7 +110,9 @@ def lib() -> C.CDLL:
         "qc_p2p_open": (C.c_int, [P, I32, P]),
         "qc_attn_partial_p2p": (C.c_int, [P, C.c_int, P, P]),
         "qc_attn_combine_p2p": (C.c_int, [P, C.c_int, P, P, P]),
+        "qc_p2p_reset": (C.c_int, [P, P]),
         "qc_attn_decode_noalloc": (C.c_int, [P, P, P, I32, P, I32, PI32, I32, P, P, P, P, P, P]),
+        "qc_attn_noalloc_check": (C.c_int, [P]),
         "qc_bfp8_packed_bytes": (C.c_int64, [I32, I32]),
         "qc_bfp8_create": (C.c_int, [C.c_int, I32, I32, C.POINTER(P)]),
         "qc_bfp8_destroy": (None, [P]),
@@ -316,6 +318,9 @@ class QCache:
     def attn_combine_p2p(self, layer, proj_ptr, out_ptr, stream=0):
         self._ck(self.L.qc_attn_combine_p2p(self.h, layer, proj_ptr, out_ptr, stream))
 
+    def p2p_reset(self, stream=0):
+        self._ck(self.L.qc_p2p_reset(self.h, stream))
+
     def attn_combine(self, partials_ptr, n_parts, proj_ptr, out_ptr, stream=0):
         self._ck(self.L.qc_attn_combine(self.h, partials_ptr, n_parts, proj_ptr, out_ptr, stream))
 
@@ -340,6 +345,14 @@ def attn_decode_noalloc(proj_ptr, k_pool_ptr, v_pool_ptr, max_pages, page_table_
                                   rope_cos_ptr, rope_sin_ptr, out_ptr, stream)
     if rc:
         raise QCacheError(rc, L.qc_last_error(None).decode())
+
+
+def attn_noalloc_check(stream=0):
+    """qc_attn_noalloc_check: raise the error the no-allocation kernels
+    recorded on the current device since the last check (and clear it)."""
+    rc = lib().qc_attn_noalloc_check(stream)
+    if rc:
+        raise QCacheError(rc, lib().qc_last_error(None).decode())
 
 
 class Bfp8Matrix:

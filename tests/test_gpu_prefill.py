@@ -98,3 +98,34 @@ def test_prefill_then_decode_continues(qcache, synth, oracle):
     ref = oracle.attn_decode(pa["proj"][T], a["q_norm"], a["k_norm"], T, kc, vc)
     assert_out_close(host_u16(o1)[0], ref, synth)
     assert q.match_prefix(s, list(range(T + 1)) + [99]) == T + 1
+
+
+@pytest.mark.parametrize("poison", [0x7F80, 0x7FC0])   # bf16 +Inf, NaN
+def test_prefill_ignores_stale_rows_of_a_reused_page(qcache, synth, oracle, poison):
+    """A page freed by one sequence and reused by the next still holds the old
+    rows past the new sequence's length.  Those rows enter the tensor-core
+    P.V tile with P = 0; even non-finite leftovers must not reach the output."""
+    T = 10
+    q = qcache.QCache(n_attn_layers=1, n_gdn_layers=1, max_seqs=2, max_pages=2, max_ctx=128,
+                      max_batch=1, max_snapshots=1, device=0)
+    a = synth.attn_inputs(820, 1, 0)
+    pa = synth.attn_inputs(821, T, 0)
+    q.set_attn_params(0, a["q_norm"], a["k_norm"])
+    old = q.seq_alloc()
+    q.seq_reserve(old, 128)
+    bad = np.full((128, 4, 256), poison, np.uint16)
+    q.kv_write(old, 0, 0, 128, dev(bad).data_ptr(), dev(bad).data_ptr())
+    torch.cuda.synchronize()
+    q.seq_free(old)
+    s = q.seq_alloc()
+    out = empty_u16(T, 4096)
+    q.prefill_begin(s, T)
+    q.attn_prefill(0, dev(pa["proj"]).data_ptr(), out.data_ptr())
+    q.prefill_end()
+    q.check_device()
+    kc = np.zeros((T, 4, 256), np.uint16)
+    vc = np.zeros((T, 4, 256), np.uint16)
+    got = host_u16(out)
+    for t in range(T):
+        ref = oracle.attn_decode(pa["proj"][t], a["q_norm"], a["k_norm"], t, kc, vc)
+        assert_out_close(got[t], ref, synth)

@@ -8,7 +8,9 @@ kernel's scratch lives in a fixed array inside the library.  This test builds
 such caller-owned buffers with the same contents as a context-managed
 sequence, runs two consecutive decode steps through both entry points and
 requires the same outputs (within the parity tolerance) and the same appended
-K/V bytes.  It sits in its own file, collected last, so a failure here stops a
+K/V bytes, and checks both against the oracle; it also checks that the
+kernels' error word reaches the caller through qc_attn_noalloc_check.  It
+sits in its own file, collected last, so a failure here stops a
 -x run only after every other test ran.
 """
 import numpy as np
@@ -18,7 +20,7 @@ pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
 
-from gpu_util import OUT_ATOL, OUT_RTOL, dev, empty_u16, host_u16  # noqa: E402
+from gpu_util import assert_f32_close, assert_out_close, dev, empty_u16, host_u16  # noqa: E402
 
 
 def test_noalloc_matches_context_decode_two_steps(qcache, synth, oracle):
@@ -66,9 +68,20 @@ def test_noalloc_matches_context_decode_two_steps(qcache, synth, oracle):
                                    max_pages, ptab.data_ptr(), pt_stride, pos, qn.data_ptr(),
                                    kn.data_ptr(), rope_c.data_ptr(), rope_s.data_ptr(),
                                    out_na.data_ptr())
+        qcache.attn_noalloc_check()
         a = synth.bf16_to_f32(host_u16(out_na))
         b_ = synth.bf16_to_f32(host_u16(out_ctx))
-        np.testing.assert_allclose(a, b_, atol=OUT_ATOL, rtol=OUT_RTOL)
+        assert_f32_close(a, b_)
+        # and both against the oracle, over the same cache contents
+        for b, L in enumerate(lens):
+            P = L + t
+            kc = np.zeros((P + 1, 4, 256), np.uint16)
+            vc = np.zeros((P + 1, 4, 256), np.uint16)
+            kp, vp = host_u16(kpool), host_u16(vpool)
+            for p in range(P):
+                kc[p], vc[p] = kp[phys[b, p // 64], :, p % 64], vp[phys[b, p // 64], :, p % 64]
+            ref = oracle.attn_decode(host_u16(proj)[b], d["q_norm"], d["k_norm"], P, kc, vc)
+            assert_out_close(host_u16(out_na)[b], ref, synth)
     q.check_device()
 
     # the appends of both steps landed in the caller's pool, bit for bit
@@ -87,3 +100,34 @@ def test_noalloc_rejects_oversized_batch(qcache):
         qcache.attn_decode_noalloc(16, 16, 16, 8, 16, 4, [0] * 65, 16, 16, 16, 16, 16)
     assert e.value.code == qcache.QC_ERR_ARG
     assert "limit" in str(e.value)
+
+
+def test_noalloc_reports_out_of_range_page(qcache, synth):
+    """A page-table entry outside [0, max_pages) makes the kernel skip that
+    tile and record QC_ERR_BOUNDS; qc_attn_noalloc_check returns it once and
+    clears it, so the next good call checks clean."""
+    n, max_pages, pt_stride, L = 1, 8, 4, 130
+    d = synth.attn_inputs(78, n, L)
+    kpool = torch.zeros(max_pages, 4, 64, 256, dtype=torch.int16, device="cuda")
+    vpool = torch.zeros_like(kpool)
+    cs = np.zeros((L + 1, 32), np.float32)
+    sn = np.zeros((L + 1, 32), np.float32)
+    rope_c, rope_s = dev(cs), dev(sn)
+    qn, kn = dev(d["q_norm"]), dev(d["k_norm"])
+    proj = dev(d["proj"])
+    out = empty_u16(n, 4096)
+    good = np.array([[3, 5, 6, 0]], np.int32)
+    bad = good.copy()
+    bad[0, 1] = max_pages                     # the second page is out of range
+    args = (kpool.data_ptr(), vpool.data_ptr(), max_pages)
+    qcache.attn_noalloc_check()               # clean start, whatever ran before
+    qcache.attn_decode_noalloc(proj.data_ptr(), *args, dev(bad).data_ptr(), pt_stride, [L],
+                               qn.data_ptr(), kn.data_ptr(), rope_c.data_ptr(),
+                               rope_s.data_ptr(), out.data_ptr())
+    with pytest.raises(qcache.QCacheError) as e:
+        qcache.attn_noalloc_check()
+    assert e.value.code == 5                  # QC_ERR_BOUNDS
+    qcache.attn_decode_noalloc(proj.data_ptr(), *args, dev(good).data_ptr(), pt_stride, [L],
+                               qn.data_ptr(), kn.data_ptr(), rope_c.data_ptr(),
+                               rope_s.data_ptr(), out.data_ptr())
+    qcache.attn_noalloc_check()
