@@ -77,8 +77,18 @@ typedef struct qc_config {
   int32_t max_ctx;         /* positions per sequence; size of the RoPE table */
   int32_t max_batch;       /* sequences per decode step */
   int32_t max_snapshots;   /* DeltaNet/conv snapshot slots of the prefix cache */
-  int32_t flags;           /* reserved, 0 */
+  int32_t flags;           /* QC_FLAG_* bits, 0 for the defaults */
 } qc_config;
+
+/* Activation math.  By default (flags 0) the kernels compute the exact
+ * functions (expf; sigmoid 1/(1+exp(-x)); SiLU x*sigmoid(x)).  With
+ * QC_FLAG_REFERENCE_MATH they compute what the reference computes, with
+ * Schraudolph's fast exp (src/engine.cpp:2349-2376) in the softplus of the
+ * decay, the beta and output-gate sigmoids and every SiLU (conv output, z
+ * gate), so outputs follow the reference engine's own results (within f32
+ * reordering) instead of the exact functions, which differ from them by up
+ * to a few percent.  Either way the cost is the same. */
+#define QC_FLAG_REFERENCE_MATH 1
 
 /* ---------------------------------------------------------------- context */
 

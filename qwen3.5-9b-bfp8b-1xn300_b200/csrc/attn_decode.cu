@@ -586,13 +586,13 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const CombineArgs c) 
     return;
   }
   const float g = bf2f(c.proj[(int64_t)b * 10240 + h * 2 * HD + HD + t]);
-  c.out[(int64_t)b * 4096 + h * HD + t] = f2bf((O / L) * sigmoid_exact(g));
+  c.out[(int64_t)b * 4096 + h * HD + t] = f2bf((O / L) * gate_sigmoid(g, c.ref_math));
 }
 
 // Cross-device merge: one CTA per head, thread = dimension.
 __global__ void __launch_bounds__(256) attn_merge_records_kernel(const float* rec, int n_parts,
                                                                  const uint16_t* proj,
-                                                                 uint16_t* out) {
+                                                                 uint16_t* out, int ref_math) {
   const int h = blockIdx.x, t = threadIdx.x;
   float M = -INFINITY;
   for (int g = 0; g < n_parts; ++g) M = fmaxf(M, rec[(g * 16 + h) * (HD + 2)]);
@@ -604,7 +604,7 @@ __global__ void __launch_bounds__(256) attn_merge_records_kernel(const float* re
     O = fmaf(f, r[2 + t], O);
   }
   const float gt = bf2f(proj[h * 2 * HD + HD + t]);
-  out[h * HD + t] = f2bf((O / L) * sigmoid_exact(gt));
+  out[h * HD + t] = f2bf((O / L) * gate_sigmoid(gt, ref_math));
 }
 
 // The cross-device merge from this rank's mailbox.  The step is done[layer] + 1
@@ -663,7 +663,7 @@ __global__ void __launch_bounds__(256) attn_merge_mailbox_kernel(const MailboxMe
     O = fmaf(f, __ldcg(r + 2 + t), O);
   }
   const float gt = bf2f(m.proj[h * 2 * HD + HD + t]);
-  m.out[h * HD + t] = f2bf((O / L) * sigmoid_exact(gt));
+  m.out[h * HD + t] = f2bf((O / L) * gate_sigmoid(gt, m.ref_math));
   __syncthreads();
   // every CTA read done[layer] at its start; the 16th to get here advances it
   if (t == 0 && atomicAdd(m.consumed + m.layer, 1u) % 16u == 15u) atomicAdd(m.done + m.layer, 1u);
@@ -677,8 +677,8 @@ cudaError_t launch_attn_merge_mailbox(const MailboxMergeArgs& m, cudaStream_t s)
 }
 
 cudaError_t launch_attn_merge_records(const float* records, int32_t n_parts, const uint16_t* proj,
-                                      uint16_t* out, cudaStream_t s) {
-  attn_merge_records_kernel<<<16, 256, 0, s>>>(records, n_parts, proj, out);
+                                      uint16_t* out, int ref_math, cudaStream_t s) {
+  attn_merge_records_kernel<<<16, 256, 0, s>>>(records, n_parts, proj, out, ref_math);
   return cudaGetLastError();
 }
 

@@ -47,6 +47,35 @@ __device__ __forceinline__ void unpack8(const uint4& w, float (&x)[8]) {
 __device__ __forceinline__ float sigmoid_exact(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float silu_exact(float x) { return x * sigmoid_exact(x); }
 
+// ------------------------------------ the reference's fast-math activations
+// With QC_FLAG_REFERENCE_MATH the kernels compute what the reference computes
+// (src/engine.cpp:2349-2376): Schraudolph's exp, i.e. clamp x to [-88, 88]
+// and reinterpret the integer 12102203 * x + 1065353216 as float bits.  The
+// scalar version (softplus, beta and gate sigmoids) converts by truncation;
+// the AVX-512 SiLU (conv output, z gate) with _mm512_cvtps_epi32, which rounds
+// to nearest even.  The reference's build (-ffast-math) contracts the
+// multiply-add into one FMA, as here.
+__device__ __forceinline__ float ref_exp_rz(float x) {
+  x = fminf(fmaxf(x, -88.0f), 88.0f);
+  return __int_as_float(__float2int_rz(fmaf(12102203.0f, x, 1065353216.0f)));
+}
+__device__ __forceinline__ float ref_exp_rn(float x) {
+  x = fminf(fmaxf(x, -88.0f), 88.0f);
+  return __int_as_float(__float2int_rn(fmaf(12102203.0f, x, 1065353216.0f)));
+}
+// the attention output gate and the DeltaNet beta (fast_sigmoidf)
+__device__ __forceinline__ float gate_sigmoid(float x, int ref) {
+  return ref ? 1.0f / (1.0f + ref_exp_rz(-x)) : sigmoid_exact(x);
+}
+// conv output and z gate (fast_silu_avx512)
+__device__ __forceinline__ float act_silu(float x, int ref) {
+  return ref ? x * (1.0f / (1.0f + ref_exp_rn(-x))) : silu_exact(x);
+}
+// the exp inside softplus (fast_expf)
+__device__ __forceinline__ float softplus_exp(float x, int ref) {
+  return ref ? ref_exp_rz(x) : expf(x);
+}
+
 // ------------------------------------------------------------ PTX wrappers
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(T) gdn_decode_kernel(const GdnArgs a) {
     y = fmaf(bf2f(ring[t1 * CONV + c]), w[CONV + c], y);
     y = fmaf(bf2f(ring[t2 * CONV + c]), w[2 * CONV + c], y);
     y = fmaf(bf2f(x[c]), w[3 * CONV + c], y);
-    return silu_exact(y);
+    return act_silu(y, a.ref_math);
   };
   // q channels kh*128 + i and k channels 2048 + kh*128 + i, i < 128
   float sq = 0.0f, sk = 0.0f;
@@ -132,9 +132,9 @@ __global__ void __launch_bounds__(T) gdn_decode_kernel(const GdnArgs a) {
 
   // ---- decay and beta (src/engine.cpp:3277-3281)
   const float biased = bf2f(x[A_OFF + vh]) + a.dt_bias[vh];
-  const float sp = (biased > 20.0f) ? biased : logf(1.0f + expf(biased));
+  const float sp = (biased > 20.0f) ? biased : logf(1.0f + softplus_exp(biased, a.ref_math));
   const float decay = expf(sp * a.ssm_a[vh]);
-  const float beta = sigmoid_exact(bf2f(x[B_OFF + vh]));
+  const float beta = gate_sigmoid(bf2f(x[B_OFF + vh]), a.ref_math);
 
   const bool ok = __syncthreads_and(mbar_wait(&s_bar, 0, a.err));
 
@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(T) gdn_decode_kernel(const GdnArgs a) {
   const float rms = 1.0f / sqrtf(tot / 128.0f + EPS);
   for (int i = tid; i < RB; i += T) {
     const int d = r * RB + i;
-    const float y = (s_o[i] * rms) * a.ssm_norm[d] * silu_exact(s_z[i]);
+    const float y = (s_o[i] * rms) * a.ssm_norm[d] * act_silu(s_z[i], a.ref_math);
     a.out[(int64_t)b * 4096 + vh * HK + d] = f2bf(y);
   }
 }
@@ -374,7 +374,7 @@ __global__ void __launch_bounds__(PTHREADS, QC_GDN_CTAS) gdn_decode_persistent(c
         y = fmaf(bf2f(ring[t2 * CONV + c]), w[2 * CONV + c], y);
         y = fmaf(bf2f(x[c]), w[3 * CONV + c], y);
       }
-      return silu_exact(y);
+      return act_silu(y, a.ref_math);
     };
     if (PRE) {
       asm volatile("cp.async.wait_all;" ::: "memory");
@@ -421,9 +421,9 @@ __global__ void __launch_bounds__(PTHREADS, QC_GDN_CTAS) gdn_decode_persistent(c
     }
     const float qs = 1.0f / sqrtf(tq + EPS), ks = 1.0f / sqrtf(tk + EPS);
     const float biased = bf2f(a_raw) + a.dt_bias[vh];
-    const float sp = (biased > 20.0f) ? biased : logf(1.0f + expf(biased));
+    const float sp = (biased > 20.0f) ? biased : logf(1.0f + softplus_exp(biased, a.ref_math));
     const float decay = expf(sp * a.ssm_a[vh]);
-    const float beta = sigmoid_exact(bf2f(b_raw));
+    const float beta = gate_sigmoid(bf2f(b_raw), a.ref_math);
     float4 k4 = reinterpret_cast<const float4*>(sm.k)[lane];
     float4 q4 = reinterpret_cast<const float4*>(sm.q)[lane];
     k4.x *= ks; k4.y *= ks; k4.z *= ks; k4.w *= ks;
@@ -492,7 +492,7 @@ __global__ void __launch_bounds__(PTHREADS, QC_GDN_CTAS) gdn_decode_persistent(c
     for (int q = 0; q < PCONSUMERS; ++q) tot += sm.red[2 * PCONSUMERS + q];
     const float rms = 1.0f / sqrtf(tot / 128.0f + EPS);
     for (int i = tid; !aborted && i < HK; i += NT) {
-      const float yy = (sm.o[i] * rms) * a.ssm_norm[i] * silu_exact(sm.z[i]);
+      const float yy = (sm.o[i] * rms) * a.ssm_norm[i] * act_silu(sm.z[i], a.ref_math);
       a.out[(int64_t)b * 4096 + vh * HK + i] = f2bf(yy);
     }
     pconsumer_sync();  // sm.q/k/v/z/o/red are rewritten by the next item

@@ -58,6 +58,7 @@ struct GdnArgs {
   const int32_t* slots;      // [n]
   const int32_t* pos;        // [n]
   int32_t n;
+  int32_t ref_math;          // 1: the reference's fast-math activations (common.cuh)
   int* err;
 };
 cudaError_t launch_gdn_decode(const GdnArgs& a, cudaStream_t s);
@@ -98,6 +99,7 @@ struct CombineArgs {
   const float* part_o;
   const int32_t* split;
   int32_t n;
+  int32_t ref_math;          // 1: the reference's fast-math gate (common.cuh)
   // when non-null: write the merged record (m, l, o unnormalised) of sequence
   // 0 as [16 heads][2 + 256] instead of the gated bf16 output
   float* record;
@@ -119,7 +121,7 @@ int attn_smem_bytes();
 // Merge n_parts records [n_parts][16][258] (m, l, o) into the gated bf16
 // output [4096] of one sequence (attn_decode.cu).
 cudaError_t launch_attn_merge_records(const float* records, int32_t n_parts, const uint16_t* proj,
-                                      uint16_t* out, cudaStream_t s);
+                                      uint16_t* out, int ref_math, cudaStream_t s);
 // The same merge from this rank's mailbox, after waiting (bounded) until every
 // rank's counter [layer][r] has reached 16 * (done[layer] + 1); the last CTA
 // to finish advances done[layer].
@@ -132,6 +134,7 @@ struct MailboxMergeArgs {
   int32_t world, layer, n_layers;
   const uint16_t* proj;
   uint16_t* out;
+  int32_t ref_math;
   int* err;
 };
 cudaError_t launch_attn_merge_mailbox(const MailboxMergeArgs& m, cudaStream_t s);
@@ -152,6 +155,7 @@ struct GdnPrefillArgs {
   float* conv_out;           // scratch [T][8192] f32: conv + SiLU outputs of the chunk
   int32_t pos0;              // position of the chunk's first token
   int32_t T;
+  int32_t ref_math;
 };
 cudaError_t launch_gdn_prefill(const GdnPrefillArgs& a, cudaStream_t s);
 
@@ -171,6 +175,7 @@ struct AttnPrefillArgs {
   int32_t pos0;
   int32_t T;
   int32_t n_split;           // CTAs per kv-head
+  int32_t ref_math;
   int* err;
 };
 cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, const CUtensorMap& tmk,

@@ -112,9 +112,9 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArg
   if (tid < T) {  // decay and beta (src/engine.cpp:3277-3281)
     const uint16_t* x = a.proj + (int64_t)tid * 12352;
     const float biased = bf2f(x[12288 + vh]) + a.dt_bias[vh];
-    const float sp = (biased > 20.0f) ? biased : logf(1.0f + expf(biased));
+    const float sp = (biased > 20.0f) ? biased : logf(1.0f + softplus_exp(biased, a.ref_math));
     sm.decay[tid] = expf(sp * a.ssm_a[vh]);
-    sm.beta[tid] = sigmoid_exact(bf2f(x[12320 + vh]));
+    sm.beta[tid] = gate_sigmoid(bf2f(x[12320 + vh]), a.ref_math);
   }
   __syncthreads();
   // L2 normalisation of q and k per token (src/engine.cpp:3261-3275)
@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(const GdnPrefillArg
     const float rms = 1.0f / sqrtf(tot / 128.0f + EPS);
     const int dd = r * GRB + d;
     const float z = bf2f(a.proj[(int64_t)t * 12352 + 8192 + vh * HK + dd]);
-    const float y = (sm.o[t][d] * rms) * a.ssm_norm[dd] * silu_exact(z);
+    const float y = (sm.o[t][d] * rms) * a.ssm_norm[dd] * act_silu(z, a.ref_math);
     a.out[(int64_t)t * 4096 + vh * HK + dd] = f2bf(y);
   }
 }
@@ -240,7 +240,7 @@ __global__ void __launch_bounds__(128) gdn_prefill_conv_kernel(const GdnPrefillA
     y = fmaf(h[1], w1, y);
     y = fmaf(h[2], w2, y);
     y = fmaf(x, w3, y);
-    a.conv_out[(int64_t)(t0 + j) * CONV + c] = silu_exact(y);
+    a.conv_out[(int64_t)(t0 + j) * CONV + c] = act_silu(y, a.ref_math);
     h[0] = h[1];
     h[1] = h[2];
     h[2] = x;
@@ -660,7 +660,7 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(const AttnPrefillA
   }
   const int h = kvh * 4 + hh;
   const float gt = bf2f(a.proj[(int64_t)t * 10240 + h * 2 * HD + HD + d]);
-  a.out[(int64_t)t * 4096 + h * HD + d] = f2bf((O / L) * sigmoid_exact(gt));
+  a.out[(int64_t)t * 4096 + h * HD + d] = f2bf((O / L) * gate_sigmoid(gt, a.ref_math));
 }
 
 }  // namespace

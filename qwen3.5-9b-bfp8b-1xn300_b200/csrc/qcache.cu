@@ -98,6 +98,7 @@ struct qc_ctx {
   int32_t job_cap = 0;
   int* dev_err = nullptr;       // error words [EK_COUNT][err_layers], see err_site
   int32_t err_layers = 1;
+  int32_t ref_math = 0;         // QC_FLAG_REFERENCE_MATH
   uint16_t* pf_q = nullptr;     // prefill: q tile [4][128][256] bf16
   float* pf_rec = nullptr;      // prefill: records [4][pf_split][128][260] f32
   float* pf_conv = nullptr;     // prefill: conv outputs [32][8192] f32
@@ -331,11 +332,13 @@ int qc_create(const qc_config* cfg, int device, qc_ctx** out) {
   if (cfg->n_attn_layers < 0 || cfg->n_gdn_layers < 0 ||
       cfg->n_attn_layers + cfg->n_gdn_layers <= 0 || cfg->max_seqs <= 0 ||
       cfg->max_pages <= 0 || cfg->max_ctx <= 0 || cfg->max_batch <= 0 ||
-      cfg->max_snapshots < 0 || cfg->max_batch > cfg->max_seqs)
+      cfg->max_snapshots < 0 || cfg->max_batch > cfg->max_seqs ||
+      (cfg->flags & ~QC_FLAG_REFERENCE_MATH) != 0)
     return QC_ERR_ARG;
   qc_ctx* c = new qc_ctx();
   c->cfg = *cfg;
   c->device = device;
+  c->ref_math = (cfg->flags & QC_FLAG_REFERENCE_MATH) ? 1 : 0;
   c->host_only = true;  // becomes false once the device pools exist
   c->pt_stride = (cfg->max_ctx + PAGE - 1) / PAGE + 1;
   c->seqs.resize(cfg->max_seqs);
@@ -826,6 +829,7 @@ int qc_attn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc
   a.grid = c->b_grid;
   a.err = err_site(c, EK_ATTN_DECODE, layer);
   qc::CombineArgs cb{};
+  cb.ref_math = c->ref_math;
   cb.proj = proj;
   cb.out = out;
   cb.seg = a.seg;
@@ -846,6 +850,7 @@ int qc_gdn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc_
   QC_NEED_DEVICE(c);
   const int32_t n = (int32_t)c->b_seq.size();
   qc::GdnArgs g{};
+  g.ref_math = c->ref_math;
   g.proj = proj;
   g.out = out;
   g.state = slot_state(c, 0, layer);
@@ -947,6 +952,7 @@ int qc_attn_prefill(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, q
   QC_NEED_DEVICE(c);
   const int64_t base = (int64_t)layer * c->cfg.max_pages * PAGE_ELEMS;
   qc::AttnPrefillArgs a{};
+  a.ref_math = c->ref_math;
   a.proj = proj;
   a.out = out;
   a.k_pool = c->k_pool + base;
@@ -977,6 +983,7 @@ int qc_gdn_prefill(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc
   if (layer < 0 || layer >= c->cfg.n_gdn_layers) return fail(c, QC_ERR_ARG, "gdn layer %d", layer);
   QC_NEED_DEVICE(c);
   qc::GdnPrefillArgs g{};
+  g.ref_math = c->ref_math;
   g.proj = proj;
   g.out = out;
   g.state = slot_state(c, c->p_seq, layer);
@@ -1292,6 +1299,7 @@ int qc_attn_partial(qc_ctx* c, int layer, const uint16_t* proj, float* partial,
   a.grid = c->nsm;
   a.err = err_site(c, EK_ATTN_DECODE, layer);
   qc::CombineArgs cb{};
+  cb.ref_math = c->ref_math;
   cb.proj = proj;
   cb.out = nullptr;
   cb.seg = a.seg;
@@ -1310,7 +1318,8 @@ int qc_attn_combine(qc_ctx* c, const float* partials, int32_t n_parts, const uin
   qc::TraceRange trace_("qc_attn_combine");
   if (!c || !partials || !proj || !out || n_parts <= 0) return QC_ERR_ARG;
   QC_NEED_DEVICE(c);
-  QC_CUDA(c, qc::launch_attn_merge_records(partials, n_parts, proj, out, (cudaStream_t)stream));
+  QC_CUDA(c, qc::launch_attn_merge_records(partials, n_parts, proj, out, c->ref_math,
+                                                  (cudaStream_t)stream));
   return QC_OK;
 }
 
@@ -1438,6 +1447,7 @@ int qc_attn_partial_p2p(qc_ctx* c, int layer, const uint16_t* proj, qc_stream st
   a.grid = c->nsm;
   a.err = err_site(c, EK_ATTN_DECODE, layer);
   qc::CombineArgs cb{};
+  cb.ref_math = c->ref_math;
   cb.proj = proj;
   cb.seg = a.seg;
   cb.part_m = c->part_m;
@@ -1467,6 +1477,7 @@ int qc_attn_combine_p2p(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* ou
   int rc = p2p_ready(c);
   if (rc) return rc;
   qc::MailboxMergeArgs m{};
+  m.ref_math = c->ref_math;
   m.rec = reinterpret_cast<const float*>(c->mbox);
   m.cnt = reinterpret_cast<const uint32_t*>(c->mbox + mbox_rec_bytes(c, c->p2p_world));
   m.done = mbox_done(c);

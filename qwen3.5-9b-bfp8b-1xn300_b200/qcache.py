@@ -18,6 +18,7 @@ LIB_PATH = os.path.join(HERE, "libqcache.so")
 HEADERS = [os.path.join(HERE, "..", "include", h) for h in ("qcache.h", "qbfp8.h", "qsample.h")]
 
 QC_OK, QC_ERR_ARG, QC_ERR_OOM, QC_ERR_CUDA, QC_ERR_TIMEOUT, QC_ERR_BOUNDS, QC_ERR_NODEVICE = range(7)
+QC_FLAG_REFERENCE_MATH = 1
 DEVICE_NONE = -1
 N_HEAD, N_HEAD_KV, HEAD_DIM = 16, 4, 256
 ATTN_PROJ, ATTN_OUT = 10240, 4096
@@ -156,10 +157,10 @@ class QCache:
     """One context on one GPU (or a host-only context with device=-1)."""
 
     def __init__(self, n_attn_layers=8, n_gdn_layers=24, max_seqs=64, max_pages=4096,
-                 max_ctx=8192, max_batch=64, max_snapshots=16, device=0):
+                 max_ctx=8192, max_batch=64, max_snapshots=16, device=0, flags=0):
         self.L = lib()
         self.cfg = Config(n_attn_layers, n_gdn_layers, max_seqs, max_pages, max_ctx, max_batch,
-                          max_snapshots, 0)
+                          max_snapshots, flags)
         h = C.c_void_p()
         rc = self.L.qc_create(C.byref(self.cfg), device, C.byref(h))
         if rc:

@@ -26,6 +26,9 @@ def test_create_rejects_bad_config(qcache):
         qcache.QCache(max_seqs=0, device=qcache.DEVICE_NONE)
     with pytest.raises(qcache.QCacheError):
         qcache.QCache(max_batch=9, max_seqs=8, device=qcache.DEVICE_NONE)
+    with pytest.raises(qcache.QCacheError):  # unknown flag bits
+        qcache.QCache(max_seqs=8, max_batch=8, device=qcache.DEVICE_NONE, flags=2)
+    host_ctx(qcache, flags=qcache.QC_FLAG_REFERENCE_MATH).close()
 
 
 def test_device_calls_fail_loudly_on_host_only(qcache):
