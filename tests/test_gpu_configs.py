@@ -295,9 +295,11 @@ def test_config3_prefix_restore_at_full_sizes(qcache, synth, oracle):
         for l in range(24):
             assert torch.equal(st[l][0], rst[l][0]) and torch.equal(st[l][1], rst[l][1]), (r, l)
     del ref_layers
-    # decode after restore: the four distinct-length requests and their sources
-    seqs = reqs[:4] + [src[i] for i in pick[:4]]
-    projs = [rand_bf16(g, 4, 10240 if kd == "a" else 12352).repeat(2, 1) for kd in stack_kinds()]
+    # decode after restore: the four distinct-length requests, then their
+    # sources, as two batches of the same layout (the split-K partition of an
+    # attention batch depends on the batch's lengths and order, so equal
+    # layouts give bit-identical outputs)
+    projs = [rand_bf16(g, 4, 10240 if kd == "a" else 12352) for kd in stack_kinds()]
     # oracle inputs of request 2 (P = 1000) in attention layer 0 and DeltaNet layer 0
     P = P_list[2]
     kd_, vd_ = empty_u16(P + 1, 4, 256), empty_u16(P + 1, 4, 256)
@@ -306,10 +308,10 @@ def test_config3_prefix_restore_at_full_sizes(qcache, synth, oracle):
     st_d, hi_d = torch.empty(32, 128, 128, device="cuda"), empty_u16(3, 8192)
     q.gdn_state_read(reqs[2], 0, st_d.data_ptr(), hi_d.data_ptr())
     st0, hist0 = host_f32(st_d).copy(), synth.bf16_to_f32(host_u16(hi_d)).copy()
-    outs = _decode_stack(q, seqs, projs)
-    for o in outs:
-        h = u16(o)
-        np.testing.assert_array_equal(h[:4], h[4:])
+    outs = _decode_stack(q, reqs[:4], projs)
+    outs_src = _decode_stack(q, [src[i] for i in pick[:4]], projs)
+    for layer, (o, o2) in enumerate(zip(outs, outs_src)):
+        np.testing.assert_array_equal(u16(o), u16(o2), err_msg=f"layer {layer}")
     ref_a = oracle.attn_decode(u16(projs[3])[2], ap[0]["q_norm"], ap[0]["k_norm"], P, kc, vc)
     assert_out_close(u16(outs[3])[2], ref_a, synth)
     ref_g = oracle.gdn_decode(u16(projs[0])[2], st0, hist0, gp[0])
