@@ -225,27 +225,29 @@ __global__ void __launch_bounds__(T) gdn_decode_kernel(const GdnArgs a) {
 
 // Persistent variant for large batches: every CTA walks work items (one
 // (sequence, v-head) each) with stride gridDim.x.  The last warp streams the
-// state of its items in 16-row chunks (8 KiB bulk copies) through a 3-deep
+// state of its items in 16-row chunks (8 KiB bulk copies) through a 4-deep
 // ring, running ahead across item boundaries, so HBM stays busy while the
 // consumer warps run the conv prologue, the delta rule and the gated RMSNorm
-// of the current head.  Six CTAs per SM: the per-head prologue is a chain of
-// dependent loads and reductions, and measured throughput rose with resident
-// CTAs (2 -> 70%, 4 -> 78%, 6 -> 81% of the measured copy bandwidth at batch
-// 64) while deeper rings with fewer CTAs did not help.
+// of the current head.  Shape, from measurement at batch 64 (fraction of the
+// measured copy bandwidth): 8 consumer warps, 6 CTAs/SM, 3 stages 0.81 — the
+// 32-register cap of that occupancy spilled; 4 consumer warps (4 rows per warp
+// and chunk, 71 registers), 5 CTAs/SM, 4 stages 0.855.  Neither giving every
+// CTA the same number of items (the last third of the CTAs otherwise gets one
+// item more), nor 7 CTAs/SM with 2 stages, nor 32-row chunks did better.
 #ifndef QC_GDN_CHUNK
 #define QC_GDN_CHUNK 16
 #endif
 constexpr int PCHUNK = QC_GDN_CHUNK;       // rows per chunk
 
 #ifndef QC_GDN_STAGES
-#define QC_GDN_STAGES 3
+#define QC_GDN_STAGES 4
 #endif
 #ifndef QC_GDN_CTAS
-#define QC_GDN_CTAS 6
+#define QC_GDN_CTAS 5
 #endif
 constexpr int PSTAGES = QC_GDN_STAGES;
 #ifndef QC_GDN_WARPS
-#define QC_GDN_WARPS 8
+#define QC_GDN_WARPS 4
 #endif
 constexpr int PCONSUMERS = QC_GDN_WARPS;
 constexpr int PTHREADS = (PCONSUMERS + 1) * 32;
