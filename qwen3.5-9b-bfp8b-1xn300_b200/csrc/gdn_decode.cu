@@ -1,23 +1,39 @@
 // gdn_decode.cu — one Gated-DeltaNet decode step, fused in a single
 // memory-bound pass (src/engine.cpp:3204-3327).
 //
-// Work split, small batches (at most 8 sequences): a cluster of R = 2 or 4 CTAs
-// per (sequence, v-head), which would otherwise leave most of the 148 SMs idle.
-// Large batches use the persistent producer/consumer kernel further down.  CTA r owns state rows
+// Small batches (at most 8 sequences): R CTAs per (sequence, v-head) — R = 4
+// for one or two sequences (a cluster), R = 1 (one 512-thread CTA per head)
+// from 3 to 8 — so that enough SMs stream.  CTA r owns state rows
 // [r*128/R, (r+1)*128/R) of the head (rows are independent in the delta rule,
 // src/engine.cpp:3284-3305).  The CTA
-//   1. starts one bulk copy (TMA, cp.async.bulk) of its 128/R x 512 B state
-//      slice into shared memory;
-//   2. meanwhile runs the causal conv (width 4) + SiLU for the 128 q and 128 k
-//      channels of k-head vh % 16 and its own v channels, and appends the new
-//      input to the conv ring;
-//   3. L2-normalises q and k, computes decay and beta;
-//   4. per row: decay, s·k, delta, rank-1 update, s·q — one float4 per lane,
-//      warp-shuffle dot products — and stores the row straight back to HBM
-//      with 128-bit stores;
+//   1. loads every small input of its prologue first (conv taps, conv
+//      weights, projection row, per-head parameters): a timeline of the
+//      kernel (globaltimer stamps per CTA, batch 8) showed these loads
+//      waiting ~5 us behind the multi-megabyte state copies when those were
+//      issued first, and ~2 us when issued before them;
+//   2. then copies its state slice into shared memory in 16-row chunks
+//      (bulk copies, one mbarrier each);
+//   3. runs the causal conv (width 4) + SiLU for the 128 q and 128 k channels
+//      of k-head vh % 16 and its own v channels, appends the new input to the
+//      conv ring, L2-normalises q and k, computes decay and beta;
+//   4. per row, as soon as its chunk has landed: decay, s·k, delta, rank-1
+//      update, s·q — one float4 per lane, warp-shuffle dot products — and
+//      stores the row straight back to HBM with 128-bit stores;
 //   5. gated RMSNorm over the head's 128 outputs (for R > 1 the CTAs of the
 //      cluster exchange their partial sums of squares through distributed
 //      shared memory with plain stores), then bf16 outputs.
+// Programmatic dependent launch: nothing the previous kernel on the stream
+// can have written is read before griddepcontrol.wait, except what no kernel
+// of the open decode step writes before this one (the host's a.early: the
+// step descriptor, this layer's ring, weights and state), so those loads and
+// the state copies overlap the previous kernel's tail.  Measured (us per
+// token and layer, batch 1 / 4 / 8): 2-CTA clusters with one 32 KiB copy
+// issued first 6.67 / 2.23 / 1.47; prologue loads first 4.78 / 1.73 / 1.20;
+// one CTA per head from 3 sequences 1.65 / 1.15; early loads under the
+// dependent launch 4.42 / 1.54 / 1.10; early state copies 4.53 / - / 1.06.
+// Large batches use the persistent producer/consumer kernel further down,
+// without the dependent launch (it measured slower there: 0.770 -> 0.814 at
+// batch 64).
 // HBM traffic per (sequence, layer): state 2 MiB read + 2 MiB written, conv
 // ring 3 x 16 KiB read + 16 KiB written, projection row 24.7 KB, output 8 KB.
 //
@@ -45,42 +61,128 @@ constexpr int B_OFF = 12320;         // beta offset
 constexpr float EPS = 1e-6f;
 constexpr float SSM_SCALE = 1.0f / 11.3137f;  // src/engine.cpp:3249
 
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+#ifndef QC_GDN_PDL_SMALL
+#define QC_GDN_PDL_SMALL 1
+#endif
+#ifndef QC_GDN_EARLY_TMA
+#define QC_GDN_EARLY_TMA 1
+#endif
+#ifndef QC_GDN_PDL_LARGE
+#define QC_GDN_PDL_LARGE 0
+#endif
+
 // R CTAs (a cluster when R > 1) per (sequence, v-head), T threads each.
 template <int R, int T>
-__global__ void __launch_bounds__(T) gdn_decode_kernel(const GdnArgs a) {
+__global__ void __launch_bounds__(T, (1024 / T > 0 ? 1024 / T : 1)) gdn_decode_kernel(const GdnArgs a) {
   constexpr int RB = HK / R;     // state rows per CTA
   constexpr int NW = T / 32;     // warps
   constexpr int RPW = RB / NW;   // rows per warp
-  static_assert(RPW >= 1 && RPW <= 32 && RB % NW == 0, "row split");
+  constexpr int QKPT = (2 * HK + T - 1) / T;    // q/k channels per thread (some idle)
+  constexpr int CR = RB < 16 ? RB : 16;         // rows per state chunk
+  constexpr int NCH = RB / CR;
+  static_assert(RPW >= 1 && RPW <= 32 && RB % NW == 0 && RB <= T &&
+                (RPW <= CR ? CR % RPW == 0 : RPW % CR == 0), "row split");
   extern __shared__ __align__(128) float s_state[];  // [RB][128]
   __shared__ __align__(16) float s_q[HK];
   __shared__ __align__(16) float s_k[HK];
   __shared__ float s_v[RB];
-  __shared__ float s_z[RB];
   __shared__ float s_o[RB];
   __shared__ float s_red[2 * NW];
   __shared__ float s_ssq[R];
-  __shared__ __align__(8) uint64_t s_bar;
+  __shared__ __align__(8) uint64_t s_bar[NCH];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = blockIdx.y;
   const int vh = blockIdx.x / R;
   const int r = blockIdx.x % R;  // == rank in the cluster (cluster dims (R,1,1))
   const int kh = vh & 15;        // kh = vh % 16 (src/engine.cpp:3254)
+  if (tid == 0) {
+    for (int c = 0; c < NCH; ++c) mbar_init(&s_bar[c], 1);
+    fence_mbar_init();
+  }
+  // Loads of what the previous kernel on the stream cannot have written (the
+  // step descriptor, this layer's conv ring and weights: no kernel of the open
+  // step writes them before this one, a.early) are issued before
+  // griddepcontrol.wait; the projection row after it.
+  if (!a.early) griddep_wait();
   const int slot = a.slots[b];
   const int pos = a.pos[b];
   float* st = a.state + slot * a.state_stride + (int64_t)vh * HK * HK + (int64_t)r * RB * HK;
   uint16_t* ring = a.ring + slot * a.ring_stride;
   const uint16_t* x = a.proj + (int64_t)b * 12352;
+  const int t0 = (pos - 3) & 3, t1 = (pos - 2) & 3, t2 = (pos - 1) & 3, tw = pos & 3;
+  const float* w = a.conv_w;
 
-  if (tid == 0) {
-    mbar_init(&s_bar, 1);
-    fence_mbar_init();
+  // ---- every small input is loaded first: these loads are on the critical
+  // path, the state copy is not (it lands while the prologue computes), and
+  // loads issued after a multi-megabyte bulk transfer queue behind it.
+  // Thread j owns q/k channels i = j + m*T (q for i < 128, k after) and, for
+  // j < RB, v channel / state row j of this CTA.
+  float qk_w[QKPT][4], qk_h[QKPT][4];
+  int qk_c[QKPT];
+  uint16_t qk_x[QKPT];
+#pragma unroll
+  for (int m = 0; m < QKPT; ++m) {
+    const int i = min(tid + m * T, 2 * HK - 1);  // idle threads repeat the last channel
+    const int c = (i < HK) ? kh * HK + i : 2048 + kh * HK + (i - HK);
+    qk_c[m] = c;
+    qk_h[m][0] = bf2f(ring[t0 * CONV + c]);
+    qk_h[m][1] = bf2f(ring[t1 * CONV + c]);
+    qk_h[m][2] = bf2f(ring[t2 * CONV + c]);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) qk_w[m][t] = w[t * CONV + c];
   }
-  __syncthreads();
+  const bool has_row = tid < RB;
+  const int cv = 4096 + vh * HK + r * RB + (has_row ? tid : 0);
+  float v_w[4], v_h[4], zf = 0.0f, nrm = 0.0f;
+  uint16_t v_x = 0;
+  if (has_row) {
+    v_h[0] = bf2f(ring[t0 * CONV + cv]);
+    v_h[1] = bf2f(ring[t1 * CONV + cv]);
+    v_h[2] = bf2f(ring[t2 * CONV + cv]);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) v_w[t] = w[t * CONV + cv];
+    nrm = a.ssm_norm[r * RB + tid];
+  }
+  const float dtb = a.dt_bias[vh], ssa = a.ssm_a[vh];
+#if QC_GDN_EARLY_TMA
+  if (a.early) {
+    __syncthreads();
+    if (tid == 0) {
+      for (int c = 0; c < NCH; ++c) {
+        mbar_arrive_expect_tx(&s_bar[c], CR * HK * 4);
+        bulk_g2s(s_state + c * CR * HK, st + c * CR * HK, CR * HK * 4, &s_bar[c]);
+      }
+    }
+  }
+#endif
+  if (a.early) griddep_wait();
+  griddep_launch();
+#pragma unroll
+  for (int m = 0; m < QKPT; ++m) {
+    qk_x[m] = x[qk_c[m]];
+    qk_h[m][3] = bf2f(qk_x[m]);
+  }
+  if (has_row) {
+    v_x = x[cv];
+    v_h[3] = bf2f(v_x);
+    zf = bf2f(x[Z_OFF + vh * HK + r * RB + tid]);
+  }
+  const float a_raw = bf2f(x[A_OFF + vh]), b_raw = bf2f(x[B_OFF + vh]);
+  __syncthreads();  // every warp has issued its loads (and the barriers are initialised)
+#if QC_GDN_EARLY_TMA
+  if (tid == 0 && !a.early) {
+#else
   if (tid == 0) {
-    mbar_arrive_expect_tx(&s_bar, RB * HK * 4);
-    bulk_g2s(s_state, st, RB * HK * 4, &s_bar);
+#endif
+    for (int c = 0; c < NCH; ++c) {
+      mbar_arrive_expect_tx(&s_bar[c], CR * HK * 4);
+      bulk_g2s(s_state + c * CR * HK, st + c * CR * HK, CR * HK * 4, &s_bar[c]);
+    }
   }
   // Split cluster barrier, first half: announces that this CTA runs, so that
   // peers may write its shared memory after their matching wait.  Relaxed:
@@ -88,30 +190,28 @@ __global__ void __launch_bounds__(T) gdn_decode_kernel(const GdnArgs a) {
   if constexpr (R > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
   // ---- conv1d + SiLU (src/engine.cpp:3204-3234), ring append
-  const int t0 = (pos - 3) & 3, t1 = (pos - 2) & 3, t2 = (pos - 1) & 3, tw = pos & 3;
-  const float* w = a.conv_w;
-  auto conv1 = [&](int c) -> float {
-    float y = bf2f(ring[t0 * CONV + c]) * w[c];
-    y = fmaf(bf2f(ring[t1 * CONV + c]), w[CONV + c], y);
-    y = fmaf(bf2f(ring[t2 * CONV + c]), w[2 * CONV + c], y);
-    y = fmaf(bf2f(x[c]), w[3 * CONV + c], y);
-    return act_silu(y, a.ref_math);
-  };
-  // q channels kh*128 + i and k channels 2048 + kh*128 + i, i < 128
   float sq = 0.0f, sk = 0.0f;
-  for (int i = tid; i < 2 * HK; i += T) {
-    const int c = (i < HK) ? kh * HK + i : 2048 + kh * HK + (i - HK);
-    const float y = conv1(c);
+#pragma unroll
+  for (int m = 0; m < QKPT; ++m) {
+    const int i = tid + m * T;
+    if (i >= 2 * HK) break;
+    float y = qk_h[m][0] * qk_w[m][0];
+    y = fmaf(qk_h[m][1], qk_w[m][1], y);
+    y = fmaf(qk_h[m][2], qk_w[m][2], y);
+    y = fmaf(qk_h[m][3], qk_w[m][3], y);
+    y = act_silu(y, a.ref_math);
     if (i < HK) { s_q[i] = y; sq = fmaf(y, y, sq); }
     else { s_k[i - HK] = y; sk = fmaf(y, y, sk); }
     // one CTA of one v-head writes each q/k channel of the ring
-    if (vh < 16 && (i & (HK - 1)) / RB == r) ring[tw * CONV + c] = x[c];
+    if (vh < 16 && (i & (HK - 1)) / RB == r) ring[tw * CONV + qk_c[m]] = qk_x[m];
   }
-  for (int i = tid; i < RB; i += T) {
-    const int cv = 4096 + vh * HK + r * RB + i;
-    s_v[i] = conv1(cv);
-    ring[tw * CONV + cv] = x[cv];
-    s_z[i] = bf2f(x[Z_OFF + vh * HK + r * RB + i]);
+  if (has_row) {
+    float y = v_h[0] * v_w[0];
+    y = fmaf(v_h[1], v_w[1], y);
+    y = fmaf(v_h[2], v_w[2], y);
+    y = fmaf(v_h[3], v_w[3], y);
+    s_v[tid] = act_silu(y, a.ref_math);
+    ring[tw * CONV + cv] = v_x;
   }
 
   // ---- L2 normalisation of q and k (src/engine.cpp:3261-3275)
@@ -131,68 +231,74 @@ __global__ void __launch_bounds__(T) gdn_decode_kernel(const GdnArgs a) {
   const float qs = 1.0f / sqrtf(tq + EPS), ks = 1.0f / sqrtf(tk + EPS);
 
   // ---- decay and beta (src/engine.cpp:3277-3281)
-  const float biased = bf2f(x[A_OFF + vh]) + a.dt_bias[vh];
+  const float biased = a_raw + dtb;
   const float sp = (biased > 20.0f) ? biased : logf(1.0f + softplus_exp(biased, a.ref_math));
-  const float decay = expf(sp * a.ssm_a[vh]);
-  const float beta = gate_sigmoid(bf2f(x[B_OFF + vh]), a.ref_math);
+  const float decay = expf(sp * ssa);
+  const float beta = gate_sigmoid(b_raw, a.ref_math);
 
-  const bool ok = __syncthreads_and(mbar_wait(&s_bar, 0, a.err));
-
-  // ---- delta rule (src/engine.cpp:3284-3305), rows of this warp
+  // ---- delta rule (src/engine.cpp:3284-3305), rows of this warp, as soon as
+  // the chunk holding them has landed
   float ssq_w = 0.0f;
+  const int row0 = warp * RPW;
+  bool ok = true;
+  for (int c = row0 / CR; ok && c * CR < row0 + RPW; ++c) ok = mbar_wait(&s_bar[c], 0, a.err);
   if (ok) {
     float4 k4 = reinterpret_cast<const float4*>(s_k)[lane];
     float4 q4 = reinterpret_cast<const float4*>(s_q)[lane];
     k4.x *= ks; k4.y *= ks; k4.z *= ks; k4.w *= ks;
     q4.x *= qs; q4.y *= qs; q4.z *= qs; q4.w *= qs;
     const float4* srow = reinterpret_cast<const float4*>(s_state);
-    float4 rr[RPW];
-    float skr[RPW];
-#pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-      float4 v = srow[(warp * RPW + i) * 32 + lane];
-      v.x *= decay; v.y *= decay; v.z *= decay; v.w *= decay;
-      rr[i] = v;
-      float d = v.x * k4.x;
-      d = fmaf(v.y, k4.y, d);
-      d = fmaf(v.z, k4.z, d);
-      d = fmaf(v.w, k4.w, d);
-      skr[i] = d;
-    }
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1)
-#pragma unroll
-      for (int i = 0; i < RPW; ++i) skr[i] += __shfl_xor_sync(FULL_MASK, skr[i], m);
-    float o[RPW];
     float4* grow = reinterpret_cast<float4*>(st);
+    constexpr int G = RPW < 4 ? RPW : 4;  // rows in flight per warp (register budget)
+#pragma unroll 1
+    for (int g0 = 0; g0 < RPW; g0 += G) {
+      float4 rr[G];
+      float skr[G];
 #pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-      const int row = warp * RPW + i;
-      const float dd = beta * (s_v[row] - skr[i]);
-      float4 v = rr[i];
-      v.x = fmaf(k4.x, dd, v.x);
-      v.y = fmaf(k4.y, dd, v.y);
-      v.z = fmaf(k4.z, dd, v.z);
-      v.w = fmaf(k4.w, dd, v.w);
-      __stcs(grow + row * 32 + lane, v);  // coalesced 512 B per row, streamed
-      float d = v.x * q4.x;
-      d = fmaf(v.y, q4.y, d);
-      d = fmaf(v.z, q4.z, d);
-      d = fmaf(v.w, q4.w, d);
-      o[i] = d;
-    }
+      for (int i = 0; i < G; ++i) {
+        float4 v = srow[(row0 + g0 + i) * 32 + lane];
+        v.x *= decay; v.y *= decay; v.z *= decay; v.w *= decay;
+        rr[i] = v;
+        float d = v.x * k4.x;
+        d = fmaf(v.y, k4.y, d);
+        d = fmaf(v.z, k4.z, d);
+        d = fmaf(v.w, k4.w, d);
+        skr[i] = d;
+      }
 #pragma unroll
-    for (int m = 16; m >= 1; m >>= 1)
+      for (int m = 16; m >= 1; m >>= 1)
 #pragma unroll
-      for (int i = 0; i < RPW; ++i) o[i] += __shfl_xor_sync(FULL_MASK, o[i], m);
+        for (int i = 0; i < G; ++i) skr[i] += __shfl_xor_sync(FULL_MASK, skr[i], m);
+      float o[G];
 #pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-      const float ov = o[i] * SSM_SCALE;
-      if (lane == i) s_o[warp * RPW + i] = ov;
-      ssq_w = fmaf(ov, ov, ssq_w);
+      for (int i = 0; i < G; ++i) {
+        const int row = row0 + g0 + i;
+        const float dd = beta * (s_v[row] - skr[i]);
+        float4 v = rr[i];
+        v.x = fmaf(k4.x, dd, v.x);
+        v.y = fmaf(k4.y, dd, v.y);
+        v.z = fmaf(k4.z, dd, v.z);
+        v.w = fmaf(k4.w, dd, v.w);
+        __stcs(grow + row * 32 + lane, v);  // coalesced 512 B per row, streamed
+        float d = v.x * q4.x;
+        d = fmaf(v.y, q4.y, d);
+        d = fmaf(v.z, q4.z, d);
+        d = fmaf(v.w, q4.w, d);
+        o[i] = d;
+      }
+#pragma unroll
+      for (int m = 16; m >= 1; m >>= 1)
+#pragma unroll
+        for (int i = 0; i < G; ++i) o[i] += __shfl_xor_sync(FULL_MASK, o[i], m);
+#pragma unroll
+      for (int i = 0; i < G; ++i) {
+        const float ov = o[i] * SSM_SCALE;
+        if (lane == i) s_o[row0 + g0 + i] = ov;
+        ssq_w = fmaf(ov, ov, ssq_w);
+      }
     }
   }
-  __syncthreads();  // s_red reuse
+  ok = __syncthreads_and(ok);  // s_red reuse
   if (lane == 0) s_red[warp] = ssq_w;
   __syncthreads();
   float part = 0.0f;
@@ -216,10 +322,9 @@ __global__ void __launch_bounds__(T) gdn_decode_kernel(const GdnArgs a) {
   }
   if (!ok) return;
   const float rms = 1.0f / sqrtf(tot / 128.0f + EPS);
-  for (int i = tid; i < RB; i += T) {
-    const int d = r * RB + i;
-    const float y = (s_o[i] * rms) * a.ssm_norm[d] * act_silu(s_z[i], a.ref_math);
-    a.out[(int64_t)b * 4096 + vh * HK + d] = f2bf(y);
+  if (has_row) {
+    const float y = (s_o[tid] * rms) * nrm * act_silu(zf, a.ref_math);
+    a.out[(int64_t)b * 4096 + vh * HK + r * RB + tid] = f2bf(y);
   }
 }
 
@@ -335,6 +440,7 @@ __global__ void __launch_bounds__(PTHREADS, QC_GDN_CTAS) gdn_decode_persistent(c
   __syncthreads();
 
   if (warp == PCONSUMERS) {  // ------------------------------------ producer
+    griddep_wait();
     if (lane != 0) return;
     int i = 0;
     for (int u = blockIdx.x; u < n_items; u += gridDim.x) {
@@ -351,6 +457,8 @@ __global__ void __launch_bounds__(PTHREADS, QC_GDN_CTAS) gdn_decode_persistent(c
   }
 
   // ----------------------------------------------------------------- consumers
+  griddep_wait();
+  griddep_launch();
   bool aborted = false;
   int i = 0;
   const float* w = a.conv_w;
@@ -523,11 +631,18 @@ cudaError_t launch_persistent(const GdnArgs& a, cudaStream_t s) {
   const bool aligned = ((reinterpret_cast<uintptr_t>(a.proj) | reinterpret_cast<uintptr_t>(a.ring) |
                          reinterpret_cast<uintptr_t>(a.conv_w)) & 15) == 0 &&
                        (a.ring_stride * 2) % 16 == 0;
-  if (aligned)
-    gdn_decode_persistent<true><<<grid, PTHREADS, sizeof(PSmem), s>>>(a);
-  else
-    gdn_decode_persistent<false><<<grid, PTHREADS, sizeof(PSmem), s>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(PTHREADS, 1, 1);
+  cfg.dynamicSmemBytes = sizeof(PSmem);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = QC_GDN_PDL_LARGE;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return aligned ? cudaLaunchKernelEx(&cfg, gdn_decode_persistent<true>, a)
+                 : cudaLaunchKernelEx(&cfg, gdn_decode_persistent<false>, a);
 }
 
 template <int R, int T>
@@ -547,13 +662,15 @@ cudaError_t launch_r(const GdnArgs& a, cudaStream_t s) {
   cfg.blockDim = dim3(T, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = R;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = QC_GDN_PDL_SMALL;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = R;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = R > 1 ? 1 : 0;
+  cfg.numAttrs = R > 1 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<R, T>, a);
 }
 
@@ -567,8 +684,23 @@ cudaError_t launch_gdn_decode(const GdnArgs& a, cudaStream_t s) {
   // Measured on B200 (us/token/layer, batch 1 / 4 / 8): clusters of 4 CTAs
   // x 256 threads 6.5 / 2.2 / 1.8; clusters of 2 x 256 6.8 / 2.07 / 1.39;
   // persistent 9.6 / 2.5 / 1.37 and best from 16 up.
-  if (a.n <= 2) return launch_r<4, 256>(a, s);
-  if (a.n <= 8) return launch_r<2, 256>(a, s);
+#ifndef QC_GDN_R_SMALL
+#define QC_GDN_R_SMALL 1
+#endif
+#ifndef QC_GDN_T_SMALL
+#define QC_GDN_T_SMALL 512
+#endif
+#ifndef QC_GDN_CLUSTER_MAX
+#define QC_GDN_CLUSTER_MAX 8
+#endif
+#ifndef QC_GDN_R_TINY
+#define QC_GDN_R_TINY 4
+#endif
+#ifndef QC_GDN_T_TINY
+#define QC_GDN_T_TINY 256
+#endif
+  if (a.n <= 2) return launch_r<QC_GDN_R_TINY, QC_GDN_T_TINY>(a, s);
+  if (a.n <= QC_GDN_CLUSTER_MAX) return launch_r<QC_GDN_R_SMALL, QC_GDN_T_SMALL>(a, s);
   return launch_persistent(a, s);
 }
 

@@ -59,6 +59,7 @@ struct GdnArgs {
   const int32_t* pos;        // [n]
   int32_t n;
   int32_t ref_math;          // 1: the reference's fast-math activations (common.cuh)
+  int32_t early;             // 1: no kernel of the open step writes this layer's state
   int* err;
 };
 cudaError_t launch_gdn_decode(const GdnArgs& a, cudaStream_t s);

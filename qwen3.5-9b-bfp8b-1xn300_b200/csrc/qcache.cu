@@ -99,6 +99,7 @@ struct qc_ctx {
   int* dev_err = nullptr;       // error words [EK_COUNT][err_layers], see err_site
   int32_t err_layers = 1;
   int32_t ref_math = 0;         // QC_FLAG_REFERENCE_MATH
+  std::vector<uint8_t> gdn_ran; // DeltaNet layers already run in the open decode step
   uint16_t* pf_q = nullptr;     // prefill: q tile [4][128][256] bf16
   float* pf_rec = nullptr;      // prefill: records [4][pf_split][128][260] f32
   float* pf_conv = nullptr;     // prefill: conv outputs [32][8192] f32
@@ -794,6 +795,7 @@ int qc_decode_begin(qc_ctx* c, const int32_t* seq_ids, int32_t n, const int32_t*
     if ((rc = stage_release(c, si, st))) return rc;
   }
   c->in_step = true;
+  c->gdn_ran.assign(std::max(c->cfg.n_gdn_layers, 1), 0);
   return QC_OK;
 }
 
@@ -865,6 +867,10 @@ int qc_gdn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc_
   g.pos = c->desc + n;
   g.n = n;
   g.err = err_site(c, EK_GDN_DECODE, layer);
+  // the kernel may read this layer's state before the previous kernel on the
+  // stream completes only if no kernel of this step has written it yet
+  g.early = c->gdn_ran[layer] ? 0 : 1;
+  c->gdn_ran[layer] = 1;
   QC_CUDA(c, qc::launch_gdn_decode(g, (cudaStream_t)stream));
   return QC_OK;
 }
