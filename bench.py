@@ -45,14 +45,17 @@ GDN_BYTES_PER_LAUNCH = 4 * 8192 * 4 + 32 * 4 * 2 + 128 * 4   # conv weights + sm
 
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
-# the dominant kernel, per sequence, from the ncu captures summarised in
-# profiles/ (captured on smaller cases, scaled by the sequences processed):
+# the dominant kernel, per sequence, from single-launch ncu captures of the
+# same kernels on smaller cases, scaled by the sequences processed:
 PROFILED_TRAFFIC_PER_SEQ = {
     "stack": ("attn", (273.006592e6 + 4.397824e6) / 16,
-              "profiles/attn_partial_stack16.md (16 sequences, scaled)"),
-    "long": ("attn", 537.116672e6 + 5.645312e6, "profiles/attn_partial_long131072.md"),
+              "ncu capture of one attention launch over 16 sequences at context 4096, scaled "
+              "to the launch's sequences"),
+    "long": ("attn", 537.116672e6 + 5.645312e6,
+             "ncu capture of one attention launch at context 131072"),
     "gdn": ("gdn", (139.216640e6 + 77.228800e6) / 64,
-            "profiles/gdn_decode_persistent_batch64.md (writes partly still in L2)"),
+            "ncu capture of one DeltaNet launch over 64 sequences (part of the state writes "
+            "was still in L2 at the launch's end)"),
 }
 
 
@@ -825,6 +828,10 @@ def gemv_cpu_baseline(budget_s=10.0, threads=None):
 
 # ------------------------------------------------------------ CPU baseline
 
+REF_BUILD = ("oracle/_ref/libref.so: src/engine.cpp cache-path blocks, g++ -O3 -ffast-math "
+             "-march=x86-64-v4 (the reference builds with clang++-20 -O3 -ffast-math "
+             "-march=native)")
+
 
 def oracle_build() -> str:
     """Which build of the timed CPU restatement this host runs."""
@@ -894,6 +901,100 @@ def cpu_baseline(budget_s: float = 12.0, threads: int | None = None):
     return us, threads, sample, t_gdn * 1e6, t_attn * 1e6
 
 
+def _ref_stack_worker(args):
+    """One process of the reference arm: the reference's own host code for the
+    cache path (oracle/_ref/libref.so, the src/engine.cpp blocks compiled
+    unchanged) runs one sequence through the 32-layer stack, token after
+    token, with its caches and state resident in the reference's own
+    file-scope vectors (24 DeltaNet slots, 8 attention caches at the context).
+    Returns (steps, seconds)."""
+    budget_s, ctx, seed = args
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ctypes as C
+
+    import ref
+    L = ref.lib()
+    rng = np.random.default_rng(seed)
+    ptr = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
+    cap = ctx + 512
+    for l in range(N_ATTN):
+        k = rng.standard_normal((ctx, 4, 256), dtype=np.float32)
+        v = rng.standard_normal((ctx, 4, 256), dtype=np.float32)
+        L.ref_set_layer(l, ptr(k), ptr(v), ctx, cap, -1, None, None)
+    for l in range(N_GDN):
+        st = (rng.standard_normal((32, 128, 128), dtype=np.float32) * 0.02)
+        hist = rng.standard_normal((3, 8192), dtype=np.float32)
+        L.ref_set_layer(-1, None, None, 0, 0, l, ptr(st), ptr(hist))
+    conv_w = (rng.standard_normal((4, 8192), dtype=np.float32) * 0.1)
+    ssm_a = -np.exp(rng.normal(-2.0, 0.5, 32)).astype(np.float32)
+    dt_bias = np.zeros(32, np.float32)
+    norm = np.ones(128, np.float32)
+    qn = np.ones(256, np.float32)
+    gproj = rng.standard_normal(12352, dtype=np.float32)
+    aproj = rng.standard_normal(10240, dtype=np.float32)
+    out = np.zeros(4096, np.float32)
+
+    def step(pos):
+        ai = gi = 0
+        for layer in range(N_LAYERS):
+            if is_attn(layer):
+                L.ref_attn_decode_resident(ai, ptr(aproj), ptr(qn), ptr(qn), pos, ptr(out))
+                ai += 1
+            else:
+                L.ref_gdn_decode_resident(gi, ptr(gproj), ptr(conv_w), ptr(ssm_a), ptr(dt_bias),
+                                          ptr(norm), ptr(out))
+                gi += 1
+
+    step(ctx)  # warm
+    t0, n = time.perf_counter(), 1
+    while time.perf_counter() - t0 < budget_s and n < cap - ctx:
+        step(ctx + n)
+        n += 1
+    return n - 1, time.perf_counter() - t0
+
+
+def reference_available() -> bool:
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    try:
+        import ref
+        return ref.available()
+    except Exception:
+        return False
+
+
+def reference_baseline(budget_s: float = 12.0, procs: int | None = None):
+    """The reference's own CPU implementation of the path on this host: P
+    processes, each one reference engine (one sequence at a time, its 4-thread
+    WorkerPool for the DeltaNet heads, src/engine.cpp:1630-1693, single-thread
+    attention), P = host cores / 4 so the pools fill the cores.  Returns
+    (us per token per layer over all processes, threads used, sample)."""
+    cores = os.cpu_count() or 1
+    procs = procs or max(1, cores // 4)
+    # one child interpreter per engine (the reference's state is process-wide);
+    # each prints (steps, seconds) as JSON; bounded by a timeout
+    kids = [subprocess.Popen([sys.executable, os.path.abspath(__file__), "--ref-worker",
+                              f"{budget_s},{CTX},{100 + i}"], stdout=subprocess.PIPE,
+                             stderr=subprocess.PIPE, text=True) for i in range(procs)]
+    res = []
+    for k in kids:
+        try:
+            out, err = k.communicate(timeout=budget_s * 4 + 120)
+        except subprocess.TimeoutExpired:
+            k.kill()
+            raise RuntimeError("reference worker timed out")
+        if k.returncode != 0:
+            raise RuntimeError("reference worker failed: " + err.strip().splitlines()[-1:][0]
+                               if err.strip() else "reference worker failed")
+        res.append(tuple(json.loads(out.strip().splitlines()[-1])))
+    steps = sum(r[0] for r in res)
+    secs = max(r[1] for r in res)
+    us = secs / (steps * N_LAYERS) * 1e6 if steps else float("inf")
+    sample = (f"{procs} process(es) x {min(r[0] for r in res)}-{max(r[0] for r in res)} decode "
+              f"tokens of one sequence through the 32-layer stack at context {CTX} "
+              f"(reference code, 4-thread pool per process)")
+    return us, procs * 4, sample
+
+
 # ----------------------------------------------------------------- output
 
 
@@ -916,7 +1017,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--collective", choices=["p2p", "nccl"], default="p2p",
                     help="config long over several GPUs: how the split-K records travel")
+    ap.add_argument("--ref-worker", default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
+    if args.ref_worker:  # one engine of the reference arm (see reference_baseline)
+        b, c, sd = args.ref_worker.split(",")
+        print(json.dumps(_ref_stack_worker((float(b), int(c), int(sd)))), flush=True)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.config == "prefix" and args.impl == "ours":
@@ -1005,16 +1111,24 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        us, cores, sample, _, _ = cpu_baseline()
-        ref_config = dict(config, timing="host wall clock of the CPU restatement of the "
-                          "reference's decode math (oracle port, all host threads) over a "
-                          "bounded sample of the workload", sharding="rank 0 only, host cores")
+        if args.config == "stack" and reference_available():
+            us, cores, sample = reference_baseline()
+            kind, build = "reference", REF_BUILD
+            what = ("the reference's own host code for the path (src/engine.cpp blocks compiled "
+                    "unchanged into oracle/_ref), one engine per process, all host cores")
+        else:
+            us, cores, sample, _, _ = cpu_baseline()
+            kind, build = "port", oracle_build()
+            what = ("the CPU restatement of the reference's decode math (oracle port, all host "
+                    "threads)")
+        ref_config = dict(config, timing=f"host wall clock of {what} over a bounded sample of "
+                          "the workload", sharding="rank 0 only, host cores")
         emit({"impl": "reference", "metric": metric, "value": round(us, 3), "unit": "us",
               "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
               "higher_is_better": False, "dtype": "f32", "data": "synthetic",
               "config": ref_config,
               "cpu_baseline": {"value": round(us, 3), "unit": "us/token/layer", "cores": cores,
-                               "kind": "port", "sample": sample, "build": oracle_build()},
+                               "kind": kind, "sample": sample, "build": build},
               "e2e": {"value": round(us, 3), "unit": "us", "h2d_bytes_per_step": 0,
                       "d2h_bytes_per_step": 0}})
         return
@@ -1081,13 +1195,23 @@ def main():
         "clocks": r["clocks"],
     }
     if not args.no_cpu_baseline and world == 1:
-        cus, cores, sample, _, _ = cpu_baseline()
-        line["cpu_baseline"] = {"value": round(cus, 3), "unit": "us/token/layer", "cores": cores,
-                                "kind": "port", "sample": sample, "build": oracle_build()}
-        # the reference's own thread count: its WorkerPool (src/engine.cpp:1631)
-        cus4, _, sample4, _, _ = cpu_baseline(budget_s=6.0, threads=4)
-        line["cpu_baseline_4_threads"] = {"value": round(cus4, 3), "unit": "us/token/layer",
-                                          "cores": 4, "kind": "port", "sample": sample4, "build": oracle_build()}
+        if args.config == "stack" and reference_available():
+            cus, cores, sample = reference_baseline(budget_s=10.0)
+            line["cpu_baseline"] = {"value": round(cus, 3), "unit": "us/token/layer",
+                                    "cores": cores, "kind": "reference", "sample": sample,
+                                    "build": REF_BUILD}
+            # the reference as it ships: one inference at a time
+            cus1, c1, sample1 = reference_baseline(budget_s=6.0, procs=1)
+            line["cpu_baseline_one_engine"] = {"value": round(cus1, 3), "unit": "us/token/layer",
+                                               "cores": c1, "kind": "reference",
+                                               "sample": sample1, "build": REF_BUILD}
+        # the restatement (the parity oracle's fast build), all host threads
+        cus, cores, sample, _, _ = cpu_baseline(budget_s=8.0)
+        line["cpu_baseline_port"] = {"value": round(cus, 3), "unit": "us/token/layer",
+                                     "cores": cores, "kind": "port", "sample": sample,
+                                     "build": oracle_build()}
+        if "cpu_baseline" not in line:
+            line["cpu_baseline"] = dict(line["cpu_baseline_port"])
     emit(line)
     if dist is not None:
         dist.destroy_process_group()

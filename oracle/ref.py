@@ -60,6 +60,12 @@ def lib() -> C.CDLL:
         L.ref_prefix_rule.restype = I
         L.ref_rope_row.argtypes = [I, P, P]
         L.ref_rope_row.restype = None
+        L.ref_set_layer.argtypes = [I, P, P, I, I, I, P, P]
+        L.ref_set_layer.restype = None
+        L.ref_gdn_decode_resident.argtypes = [I, P, P, P, P, P, P]
+        L.ref_gdn_decode_resident.restype = None
+        L.ref_attn_decode_resident.argtypes = [I, P, P, P, I, P]
+        L.ref_attn_decode_resident.restype = None
         L.ref_fast_expf.argtypes = [C.c_float]
         L.ref_fast_expf.restype = C.c_float
         _lib = L

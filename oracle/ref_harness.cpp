@@ -143,6 +143,70 @@ void ref_attn_decode(const float* qkv_in, const float* q_norm, const float* k_no
   std::memcpy(out, g_attn_out.data(), sizeof(float) * MC::n_head * MC::head_dim);
 }
 
+// Resident variants for timing the reference: the caches and state stay in
+// the reference's own file-scope vectors between calls, as in the engine, so
+// a timed call does only the work of the cited block.
+//   ref_set_layer: stands up attention cache `attn_idx` (< 8) with rows
+//     [0, n) of k/v ([n][4][256] f32, capacity cap rows) and DeltaNet slot
+//     `ssm_idx` (< 24) with state and conv history (either part may be NULL).
+void ref_set_layer(int attn_idx, const float* k, const float* v, int n, int cap, int ssm_idx,
+                   const float* state, const float* conv) {
+  std::lock_guard<std::mutex> lk(g_call);
+  if (k && v && attn_idx >= 0 && attn_idx < 8) {
+    g_k_cache[attn_idx].assign((size_t)cap * kv_dim, 0.0f);
+    g_v_cache[attn_idx].assign((size_t)cap * kv_dim, 0.0f);
+    std::memcpy(g_k_cache[attn_idx].data(), k, sizeof(float) * n * kv_dim);
+    std::memcpy(g_v_cache[attn_idx].data(), v, sizeof(float) * n * kv_dim);
+  }
+  if (state && conv && ssm_idx >= 0 && ssm_idx < 24) {
+    const size_t ns = (size_t)ssm_n_v_heads * ssm_head_k_dim * ssm_head_v_dim_c;
+    g_ssm_state[ssm_idx].assign(state, state + ns);
+    g_conv_state[ssm_idx].assign(conv, conv + (size_t)conv_state_len * MC::ssm_conv_channels);
+  }
+}
+
+// The DeltaNet block on resident slot `ssm_idx_in`; weights as in ref_gdn_decode.
+void ref_gdn_decode_resident(int ssm_idx_in, const float* proj, const float* conv_w_t,
+                             const float* ssm_a, const float* dt_bias, const float* ssm_norm,
+                             float* out) {
+  start_pool();
+  std::lock_guard<std::mutex> lk(g_call);
+  using Clock = std::chrono::high_resolution_clock;
+  const int ssm_idx = ssm_idx_in;
+  static GdnHostWeights lw;  // the engine keeps them resident too
+  lw.ssm_conv1d_host.assign(conv_w_t, conv_w_t + 4 * MC::ssm_conv_channels);
+  lw.ssm_a_host.assign(ssm_a, ssm_a + MC::ssm_dt_rank);
+  lw.ssm_dt_bias_host.assign(dt_bias, dt_bias + MC::ssm_dt_rank);
+  lw.ssm_norm_host.assign(ssm_norm, ssm_norm + MC::ssm_head_v_dim);
+  std::memcpy(g_proj.data(), proj, sizeof(float) * g_combined_rows);
+  {
+#include "gdn_decode.inc"
+  }
+  std::memcpy(out, g_ssm_proj_in.data(), sizeof(float) * MC::ssm_d_inner);
+}
+
+// The attention block on resident cache `attn_idx_in` at position pos_in
+// (capacity must exceed pos_in).
+void ref_attn_decode_resident(int attn_idx_in, const float* qkv_in, const float* q_norm,
+                              const float* k_norm, int pos_in, float* out) {
+  std::lock_guard<std::mutex> lk(g_call);
+  using Clock = std::chrono::high_resolution_clock;
+  const int attn_idx = attn_idx_in;
+  const int pos = pos_in;
+  ensure_rope(pos + 1);
+  AttnHostWeights aw;
+  aw.q_norm.assign(q_norm, q_norm + MC::head_dim);
+  aw.k_norm.assign(k_norm, k_norm + MC::head_dim);
+  constexpr int q_dim = MC::n_head * MC::head_dim * 2;
+  constexpr int kv_dim_one = MC::n_head_kv * MC::head_dim;
+  float* qkv = g_qkv.data();
+  std::memcpy(qkv, qkv_in, sizeof(float) * g_qkv_rows);
+  {
+#include "attn_decode.inc"
+  }
+  std::memcpy(out, g_attn_out.data(), sizeof(float) * MC::n_head * MC::head_dim);
+}
+
 // The prefix rule of generate() (src/engine.cpp:4059-4077) against a cached
 // token list.  Returns the reused prefix length; *resets = how many times the
 // block called reset_state() (0 or 1).
