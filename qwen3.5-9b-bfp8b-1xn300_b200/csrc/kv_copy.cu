@@ -59,6 +59,7 @@ __global__ void __launch_bounds__(128) kv_gather_kernel(const uint16_t* k_pool,
 #ifndef QC_BULK_CTAS
 #define QC_BULK_CTAS 4
 #endif
+
 constexpr int BULK_STAGES = QC_BULK_STAGES;
 
 __device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {

@@ -221,15 +221,37 @@ int stage_release(qc_ctx* c, int i, cudaStream_t s) {
 
 // Upload every dirty page-table row.
 int sync_rows(qc_ctx* c, cudaStream_t s) {
+  // the dirty rows go up as one copy of the span that holds them when it fits
+  // the staging buffer (a batched restore dirties one row per request), else
+  // row by row
+  int64_t lo = -1, hi = -1;
+  for (size_t i = 0; i < c->seqs.size(); ++i)
+    if (c->seqs[i].live && c->seqs[i].dirty) {
+      if (lo < 0) lo = (int64_t)i;
+      hi = (int64_t)i;
+    }
+  if (lo < 0) return QC_OK;
+  const size_t row_bytes = (size_t)c->pt_stride * sizeof(int32_t);
+  const size_t span = (size_t)(hi - lo + 1) * row_bytes;
+  if (span <= c->stage_cap) {
+    char* buf = nullptr;
+    int si = 0;
+    if (int rc0 = stage_acquire(c, span, &buf, &si)) return rc0;
+    std::memcpy(buf, &c->h_page_table[lo * c->pt_stride], span);
+    QC_CUDA(c, cudaMemcpyAsync(c->page_table + lo * c->pt_stride, buf, span,
+                               cudaMemcpyHostToDevice, s));
+    if (int rc = stage_release(c, si, s)) return rc;
+    for (int64_t i = lo; i <= hi; ++i) c->seqs[i].dirty = false;
+    return QC_OK;
+  }
   for (size_t i = 0; i < c->seqs.size(); ++i) {
     Seq& q = c->seqs[i];
     if (!q.live || !q.dirty) continue;
-    const size_t bytes = (size_t)c->pt_stride * sizeof(int32_t);
     char* buf = nullptr;
     int si = 0;
-    if (int rc0 = stage_acquire(c, bytes, &buf, &si)) return rc0;
-    std::memcpy(buf, &c->h_page_table[i * c->pt_stride], bytes);
-    QC_CUDA(c, cudaMemcpyAsync(c->page_table + i * c->pt_stride, buf, bytes,
+    if (int rc0 = stage_acquire(c, row_bytes, &buf, &si)) return rc0;
+    std::memcpy(buf, &c->h_page_table[i * c->pt_stride], row_bytes);
+    QC_CUDA(c, cudaMemcpyAsync(c->page_table + i * c->pt_stride, buf, row_bytes,
                                cudaMemcpyHostToDevice, s));
     int rc = stage_release(c, si, s);
     if (rc) return rc;
