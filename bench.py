@@ -412,10 +412,14 @@ def run_ours(args, rank, world, dist, kinds, n_total, ctx):
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
 
     vals = torch.tensor([ms, e2e_ms, attn_ms, gdn_ms], device="cuda", dtype=torch.float64)
+    rank_ms = [ms]
     if dist is not None:
+        every = [torch.zeros_like(vals) for _ in range(world)]
+        dist.all_gather(every, vals)
+        rank_ms = [float(v[0]) for v in every]   # each rank's own step time
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     ms, e2e_ms, attn_ms, gdn_ms = vals.tolist()
-    return dict(ms=ms, e2e_ms=e2e_ms, attn_ms=attn_ms, gdn_ms=gdn_ms,
+    return dict(ms=ms, e2e_ms=e2e_ms, attn_ms=attn_ms, gdn_ms=gdn_ms, rank_ms=rank_ms,
                 attn_layer_bytes=attn_b / args.steps, gdn_layer_bytes=gdn_b / args.steps,
                 n_local=n, h2d=h2d, d2h=d2h, clocks=clk,
                 l2="L2 flushed (512 MB write) between steps" if small
@@ -1207,6 +1211,7 @@ def main():
                  "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]}
                 if r["e2e_ms"] is not None else None),
         "gpu_launches": args.steps * (n_gdn + 2 * n_attn),
+        "rank_ms_per_step": [round(x, 4) for x in r.get("rank_ms", [r["ms"]])],
         "clocks": r["clocks"],
     }
     if not args.no_cpu_baseline and world == 1:
