@@ -295,14 +295,19 @@ def run_ours(args, rank, world, dist, kinds, n_total, ctx):
     stack.q.decode_abort()
     torch.cuda.synchronize()
 
-    def graph_step():
+    def graph_step(kev=None):
         stack.q.decode_begin(stack.seqs, stream=stream)
+        if kev is not None:
+            kev[0].record()
         graph.replay()
+        if kev is not None:
+            kev[1].record()
         stack.q.decode_end()
 
     # ---- device-timed region: K graph steps
     attn_b = gdn_b = 0
     sev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    kev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.5)   # let the sampler come up before the timed region
@@ -317,7 +322,7 @@ def run_ours(args, rank, world, dist, kinds, n_total, ctx):
         if flush_buf is not None:
             flush_buf.zero_()
         sev[k][0].record()
-        graph_step()
+        graph_step(kev[k])
         sev[k][1].record()
     t1.record()
     barrier()
@@ -325,6 +330,9 @@ def run_ours(args, rank, world, dist, kinds, n_total, ctx):
     # with L2 flushes inside the region, the step time is the sum of the steps
     ms = (sum(e0.elapsed_time(e1) for e0, e1 in sev) / args.steps if small
           else t0.elapsed_time(t1) / args.steps)
+    # the layer kernels alone (the graph replay), without qc_decode_begin's
+    # descriptor upload: what small configurations spend in their kernels
+    kernels_ms = sum(e0.elapsed_time(e1) for e0, e1 in kev) / args.steps
     # per-layer-type split: with one layer type it is the step; otherwise a few
     # extra non-graph steps with an event pair around every layer call (the
     # GPU stays saturated in these workloads, so the split is device time)
@@ -411,15 +419,17 @@ def run_ours(args, rank, world, dist, kinds, n_total, ctx):
     barrier()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
 
-    vals = torch.tensor([ms, e2e_ms, attn_ms, gdn_ms], device="cuda", dtype=torch.float64)
+    vals = torch.tensor([ms, e2e_ms, attn_ms, gdn_ms, kernels_ms], device="cuda",
+                        dtype=torch.float64)
     rank_ms = [ms]
     if dist is not None:
         every = [torch.zeros_like(vals) for _ in range(world)]
         dist.all_gather(every, vals)
         rank_ms = [float(v[0]) for v in every]   # each rank's own step time
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, attn_ms, gdn_ms = vals.tolist()
+    ms, e2e_ms, attn_ms, gdn_ms, kernels_ms = vals.tolist()
     return dict(ms=ms, e2e_ms=e2e_ms, attn_ms=attn_ms, gdn_ms=gdn_ms, rank_ms=rank_ms,
+                kernels_ms=kernels_ms,
                 attn_layer_bytes=attn_b / args.steps, gdn_layer_bytes=gdn_b / args.steps,
                 n_local=n, h2d=h2d, d2h=d2h, clocks=clk,
                 l2="L2 flushed (512 MB write) between steps" if small
@@ -1212,6 +1222,8 @@ def main():
                 if r["e2e_ms"] is not None else None),
         "gpu_launches": args.steps * (n_gdn + 2 * n_attn),
         "rank_ms_per_step": [round(x, 4) for x in r.get("rank_ms", [r["ms"]])],
+        "layer_kernels_ms_per_step": (round(r["kernels_ms"], 4) if r.get("kernels_ms")
+                                      is not None else None),
         "clocks": r["clocks"],
     }
     if not args.no_cpu_baseline and world == 1:
