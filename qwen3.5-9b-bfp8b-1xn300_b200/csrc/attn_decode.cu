@@ -184,6 +184,14 @@ __device__ __forceinline__ TileInfo tile_info(const AttnArgs& a, const Cursor& c
   return t;
 }
 
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+#ifndef QC_ATTN_PDL
+#define QC_ATTN_PDL 1
+#endif
+
 __global__ void __launch_bounds__(THREADS, 1)
     attn_partial_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv) {
@@ -191,10 +199,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                       ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Programmatic dependent launch: with a.early the step descriptor, the
+  // page table and this layer's cached K/V cannot have been written by the
+  // previous kernel on the stream (nothing of the open step writes them
+  // before this layer's own call), so the producer streams K/V while that
+  // kernel drains; the projection rows, the append and the records wait.
+  if (!a.early) griddep_wait();
   const int total = a.split[0], per = a.split[1];
   const int u_begin = blockIdx.x * per;
   const int u_end = min(total, u_begin + per);
-  if (u_begin >= u_end) return;
+  if (u_begin >= u_end) {
+    griddep_wait();  // every thread: the grid completes after its predecessor
+    return;
+  }
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -246,13 +263,19 @@ __global__ void __launch_bounds__(THREADS, 1)
               }
           }
         }
-        if (!__shfl_sync(FULL_MASK, ok, 0)) return;
+        if (!__shfl_sync(FULL_MASK, ok, 0)) {
+          griddep_wait();
+          return;
+        }
       }
     }
+    griddep_wait();
     return;
   }
 
   // -------------------------------------------------------------- consumers
+  griddep_wait();
+  griddep_launch();
   const int g = lane >> 2, t4 = lane & 3;
   Cursor c;
   c.seek(a, u_begin);
@@ -529,6 +552,8 @@ __device__ __forceinline__ void publish_record(const CombineArgs& c, int h, floa
 __global__ void __launch_bounds__(256) attn_combine_kernel(const CombineArgs c) {
   __shared__ float s_w[512];
   __shared__ float s_red[8];
+  griddep_wait();  // the partial records of the kernel before
+  griddep_launch();
   const int pair = blockIdx.x, hh = blockIdx.y;
   const int b = pair >> 2, kvh = pair & 3, t = threadIdx.x;
   const int np = (c.seg[b + 1] - c.seg[b]) >> 2;
@@ -697,11 +722,25 @@ cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CU
     if (e != cudaSuccess) return e;
     configured.mark(dev);
   }
-  attn_partial_kernel<<<a.grid, THREADS, attn_smem_bytes(), s>>>(a, tmk, tmv);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = QC_ATTN_PDL;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.grid, 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = attn_smem_bytes();
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_partial_kernel, a, tmk, tmv);
   if (e != cudaSuccess) return e;
-  attn_combine_kernel<<<dim3(c.n * 4, 4), 256, 0, s>>>(c);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cc = {};
+  cc.gridDim = dim3(c.n * 4, 4, 1);
+  cc.blockDim = dim3(256, 1, 1);
+  cc.stream = s;
+  cc.attrs = attr;
+  cc.numAttrs = 1;
+  return cudaLaunchKernelEx(&cc, attn_combine_kernel, c);
 }
 
 }  // namespace qc

@@ -87,6 +87,8 @@ struct AttnArgs {
   const int32_t* split;      // [2] page-heads in the batch, page-heads per CTA
   int32_t n;
   int32_t grid;              // CTAs (the SM count; CTAs past the work exit)
+  int32_t early;             // 1: no kernel of the open step writes this layer's K/V pool,
+                             //    the page table or the descriptor before this launch
   int* err;
 };
 // Combine the partials of each (sequence, kv-head) pair, apply the gate and

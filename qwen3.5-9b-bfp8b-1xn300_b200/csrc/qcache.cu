@@ -100,6 +100,7 @@ struct qc_ctx {
   int32_t err_layers = 1;
   int32_t ref_math = 0;         // QC_FLAG_REFERENCE_MATH
   std::vector<uint8_t> gdn_ran; // DeltaNet layers already run in the open decode step
+  std::vector<uint8_t> attn_ran;// attention layers already run in the open decode step
   uint16_t* pf_q = nullptr;     // prefill: q tile [4][128][256] bf16
   float* pf_rec = nullptr;      // prefill: records [4][pf_split][128][260] f32
   float* pf_conv = nullptr;     // prefill: conv outputs [32][8192] f32
@@ -818,6 +819,7 @@ int qc_decode_begin(qc_ctx* c, const int32_t* seq_ids, int32_t n, const int32_t*
   }
   c->in_step = true;
   c->gdn_ran.assign(std::max(c->cfg.n_gdn_layers, 1), 0);
+  c->attn_ran.assign(std::max(c->cfg.n_attn_layers, 1), 0);
   return QC_OK;
 }
 
@@ -852,6 +854,10 @@ int qc_attn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc
   a.n = n;
   a.grid = c->b_grid;
   a.err = err_site(c, EK_ATTN_DECODE, layer);
+  // K/V streams before the previous kernel completes only if this layer's
+  // pool has not been written in this step (its own call appends)
+  a.early = c->attn_ran[layer] ? 0 : 1;
+  c->attn_ran[layer] = 1;
   qc::CombineArgs cb{};
   cb.ref_math = c->ref_math;
   cb.proj = proj;
@@ -1326,6 +1332,10 @@ int qc_attn_partial(qc_ctx* c, int layer, const uint16_t* proj, float* partial,
   a.n = 1;
   a.grid = c->nsm;
   a.err = err_site(c, EK_ATTN_DECODE, layer);
+  // K/V streams before the previous kernel completes only if this layer's
+  // pool has not been written in this step (its own call appends)
+  a.early = c->attn_ran[layer] ? 0 : 1;
+  c->attn_ran[layer] = 1;
   qc::CombineArgs cb{};
   cb.ref_math = c->ref_math;
   cb.proj = proj;
@@ -1474,6 +1484,10 @@ int qc_attn_partial_p2p(qc_ctx* c, int layer, const uint16_t* proj, qc_stream st
   a.n = 1;
   a.grid = c->nsm;
   a.err = err_site(c, EK_ATTN_DECODE, layer);
+  // K/V streams before the previous kernel completes only if this layer's
+  // pool has not been written in this step (its own call appends)
+  a.early = c->attn_ran[layer] ? 0 : 1;
+  c->attn_ran[layer] = 1;
   qc::CombineArgs cb{};
   cb.ref_math = c->ref_math;
   cb.proj = proj;
