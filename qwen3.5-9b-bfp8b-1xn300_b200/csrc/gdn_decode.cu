@@ -65,6 +65,9 @@ __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wa
 __device__ __forceinline__ void griddep_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+#ifndef QC_GDN_MINB
+#define QC_GDN_MINB(T) (1024 / (T) > 0 ? 1024 / (T) : 1)
+#endif
 #ifndef QC_GDN_PDL_SMALL
 #define QC_GDN_PDL_SMALL 1
 #endif
@@ -77,7 +80,7 @@ __device__ __forceinline__ void griddep_launch() {
 
 // R CTAs (a cluster when R > 1) per (sequence, v-head), T threads each.
 template <int R, int T>
-__global__ void __launch_bounds__(T, (1024 / T > 0 ? 1024 / T : 1)) gdn_decode_kernel(const GdnArgs a) {
+__global__ void __launch_bounds__(T, QC_GDN_MINB(T)) gdn_decode_kernel(const GdnArgs a) {
   constexpr int RB = HK / R;     // state rows per CTA
   constexpr int NW = T / 32;     // warps
   constexpr int RPW = RB / NW;   // rows per warp
@@ -493,18 +496,18 @@ __global__ void __launch_bounds__(PTHREADS, QC_GDN_CTAS) gdn_decode_persistent(c
     // ---- prologue: conv + SiLU of the head's q, k and v channels
     constexpr int NT = PCONSUMERS * 32;
     float sq = 0.0f, sk = 0.0f;
-    for (int i = tid; i < 2 * HK; i += NT) {
-      const int c = (i < HK) ? kh * HK + i : 2048 + kh * HK + (i - HK);
-      const float y = conv1(c, i);
-      if (vh < 16) ring[tw * CONV + c] = PRE ? sm.x[i] : x[c];
-      if (i < HK) { sm.q[i] = y; sq = fmaf(y, y, sq); }
-      else { sm.k[i - HK] = y; sk = fmaf(y, y, sk); }
+    for (int t = tid; t < 2 * HK; t += NT) {
+      const int c = (t < HK) ? kh * HK + t : 2048 + kh * HK + (t - HK);
+      const float y = conv1(c, t);
+      if (vh < 16) ring[tw * CONV + c] = PRE ? sm.x[t] : x[c];
+      if (t < HK) { sm.q[t] = y; sq = fmaf(y, y, sq); }
+      else { sm.k[t - HK] = y; sk = fmaf(y, y, sk); }
     }
-    for (int i = tid; i < HK; i += NT) {
-      const int cv = 4096 + vh * HK + i;
-      sm.v[i] = conv1(cv, 2 * HK + i);
-      ring[tw * CONV + cv] = PRE ? sm.x[2 * HK + i] : x[cv];
-      sm.z[i] = bf2f(PRE ? sm.x[3 * HK + i] : x[Z_OFF + vh * HK + i]);
+    for (int t = tid; t < HK; t += NT) {
+      const int cv = 4096 + vh * HK + t;
+      sm.v[t] = conv1(cv, 2 * HK + t);
+      ring[tw * CONV + cv] = PRE ? sm.x[2 * HK + t] : x[cv];
+      sm.z[t] = bf2f(PRE ? sm.x[3 * HK + t] : x[Z_OFF + vh * HK + t]);
     }
     uint16_t a_raw, b_raw;
     if (PRE) {
@@ -601,9 +604,9 @@ __global__ void __launch_bounds__(PTHREADS, QC_GDN_CTAS) gdn_decode_persistent(c
 #pragma unroll
     for (int q = 0; q < PCONSUMERS; ++q) tot += sm.red[2 * PCONSUMERS + q];
     const float rms = 1.0f / sqrtf(tot / 128.0f + EPS);
-    for (int i = tid; !aborted && i < HK; i += NT) {
-      const float yy = (sm.o[i] * rms) * a.ssm_norm[i] * act_silu(sm.z[i], a.ref_math);
-      a.out[(int64_t)b * 4096 + vh * HK + i] = f2bf(yy);
+    for (int t = tid; !aborted && t < HK; t += NT) {
+      const float yy = (sm.o[t] * rms) * a.ssm_norm[t] * act_silu(sm.z[t], a.ref_math);
+      a.out[(int64_t)b * 4096 + vh * HK + t] = f2bf(yy);
     }
     pconsumer_sync();  // sm.q/k/v/z/o/red are rewritten by the next item
   }
