@@ -375,7 +375,8 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-constexpr int TC_SOFTMAX = 4;                  // warps: one query row per thread
+// warps 0-3: softmax (one query row per thread); warp 4 issues the MMAs,
+// warp 5 the TMA loads
 constexpr int TC_MMA_WARP = 4, TC_TMA_WARP = 5;
 constexpr int TC_THREADS = 6 * 32;
 constexpr uint32_t TMEM_COLS = 512;            // S x 2 (64 each) + O (256)
