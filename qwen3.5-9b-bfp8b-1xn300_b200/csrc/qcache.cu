@@ -673,6 +673,9 @@ int qc_kv_write(qc_ctx* c, int32_t s, int layer, int32_t pos0, int32_t n, const 
   cudaStream_t st = (cudaStream_t)stream;
   if ((rc = sync_rows(c, st))) return rc;
   const int64_t base = (int64_t)layer * c->cfg.max_pages * PAGE_ELEMS;
+  // a write inside an open step: this layer's attention call of the step must
+  // not read its pool before this copy completes (see AttnArgs::early)
+  if (c->in_step) c->attn_ran[layer] = 1;
   QC_CUDA(c, qc::launch_kv_scatter(c->k_pool + base, c->v_pool + base,
                                    c->page_table + (int64_t)s * c->pt_stride, pos0, n, k, v,
                                    c->cfg.max_pages, err_site(c, EK_KV_COPY, layer), st));
@@ -701,6 +704,9 @@ int qc_gdn_state_write(qc_ctx* c, int32_t s, int layer, const float* state,
   if (layer < 0 || layer >= c->cfg.n_gdn_layers) return fail(c, QC_ERR_ARG, "gdn layer %d", layer);
   QC_NEED_DEVICE(c);
   cudaStream_t st = (cudaStream_t)stream;
+  // a write inside an open step: this layer's DeltaNet call of the step must
+  // not read the state before the write completes (see GdnArgs::early)
+  if (c->in_step) c->gdn_ran[layer] = 1;
   QC_CUDA(c, cudaMemcpyAsync(slot_state(c, s, layer), state, (size_t)QC_GDN_STATE * 4,
                              cudaMemcpyDeviceToDevice, st));
   QC_CUDA(c, qc::launch_hist_to_ring(conv, c->seqs[s].len, slot_ring(c, s, layer), st));
