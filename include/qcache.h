@@ -171,7 +171,13 @@ int qc_decode_end(qc_ctx* ctx);
  * a step after an error.  The layer calls read the step's positions and split
  * sizes from device memory written by qc_decode_begin, so a captured graph of
  * them replays correctly after every later qc_decode_begin for the same
- * sequence list. */
+ * sequence list.  Layer kernels of a step read their own layer's KV pool and
+ * DeltaNet state while the previous kernel on the stream is still draining
+ * (programmatic dependent launch) when nothing of the step has written them
+ * yet; a write through qc_kv_write / qc_gdn_state_write inside an open step
+ * turns that off for the layer.  A captured graph keeps the choice made at
+ * capture, so do not replay it with such a write between qc_decode_begin and
+ * the replay. */
 int qc_decode_abort(qc_ctx* ctx);
 
 /* ------------------------------------------------------------------ prefill */
