@@ -535,10 +535,12 @@ __device__ __forceinline__ void publish_record(const CombineArgs& c, int h, floa
   const int par = (int)((c.done[c.layer] + 1u) & 1u);  // this step's mailbox half
   const int64_t off =
       ((((int64_t)par * c.n_layers + c.layer) * c.world + c.rank) * 16 + h) * (HD + 2);
-  for (int r = 0; r < c.world; ++r) {
-    float* rec = c.mbox_rec[r] + off;
-    if (t == 0) { rec[0] = m; rec[1] = l; }
-    rec[2 + t] = o;
+  if (t < HD) {
+    for (int r = 0; r < c.world; ++r) {
+      float* rec = c.mbox_rec[r] + off;
+      if (t == 0) { rec[0] = m; rec[1] = l; }
+      rec[2 + t] = o;
+    }
   }
   __threadfence_system();
   __syncthreads();
@@ -548,10 +550,15 @@ __device__ __forceinline__ void publish_record(const CombineArgs& c, int h, floa
 // One CTA per (sequence, kv-head pair, head of the group); the slots of the
 // CTAs that covered the pair (at most one per SM, plus one) are weighed in
 // parallel first, so the per-dimension merge below is a chain of independent
-// loads rather than a serial max/sum walk.
-__global__ void __launch_bounds__(256) attn_combine_kernel(const CombineArgs c) {
+// loads rather than a serial max/sum walk.  G groups of 256 threads split
+// that chain (group g takes slots g, g + G, ...): with few sequences a pair
+// has dozens of slots and the chain's L2 latency is the kernel's time.
+template <int G>
+__global__ void __launch_bounds__(256 * G) attn_combine_kernel(const CombineArgs c) {
+  constexpr int NT = 256 * G, NW = NT / 32;
   __shared__ float s_w[512];
-  __shared__ float s_red[8];
+  __shared__ float s_red[NW];
+  __shared__ float s_o[G > 1 ? G - 1 : 1][HD];
   griddep_wait();  // the partial records of the kernel before
   griddep_launch();
   const int pair = blockIdx.x, hh = blockIdx.y;
@@ -566,24 +573,24 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const CombineArgs c) 
     }
     float* rec = c.record + (kvh * 4 + hh) * (HD + 2);
     if (t == 0) { rec[0] = -INFINITY; rec[1] = 0.0f; }
-    rec[2 + t] = 0.0f;
+    if (t < HD) rec[2 + t] = 0.0f;
     return;
   }
   const int c0 = u0 / per, ns = (u0 + np - 1) / per - c0 + 1;
   const int base = pair + c0;
   // max over the slots
   float m = -INFINITY;
-  for (int k = t; k < ns; k += 256) m = fmaxf(m, c.part_m[(base + k) * 4 + hh]);
+  for (int k = t; k < ns; k += NT) m = fmaxf(m, c.part_m[(base + k) * 4 + hh]);
   m = warp_max(m);
   if ((t & 31) == 0) s_red[t >> 5] = m;
   __syncthreads();
   float M = s_red[0];
 #pragma unroll
-  for (int w = 1; w < 8; ++w) M = fmaxf(M, s_red[w]);
+  for (int w = 1; w < NW; ++w) M = fmaxf(M, s_red[w]);
   __syncthreads();
   // slot weights and the softmax sum
   float l = 0.0f;
-  for (int k = t; k < ns; k += 256) {
+  for (int k = t; k < ns; k += NT) {
     const float mk = c.part_m[(base + k) * 4 + hh];
     const float f = (mk == -INFINITY) ? 0.0f : exp2f(mk - M);
     s_w[k] = f;
@@ -594,24 +601,34 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const CombineArgs c) 
   __syncthreads();
   float L = 0.0f;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) L += s_red[w];
+  for (int w = 0; w < NW; ++w) L += s_red[w];
+  const int d = t & (HD - 1), g = t / HD;
   float O = 0.0f;
-  const float* po = c.part_o + ((int64_t)base * 4 + hh) * HD + t;
+  const float* po = c.part_o + ((int64_t)base * 4 + hh) * HD + d;
 #pragma unroll 8
-  for (int k = 0; k < ns; ++k) O = fmaf(s_w[k], po[(int64_t)k * 4 * HD], O);
+  for (int k = g; k < ns; k += G) O = fmaf(s_w[k], po[(int64_t)k * 4 * HD], O);
+  if constexpr (G > 1) {
+    if (g > 0) s_o[g - 1][d] = O;
+    __syncthreads();
+    if (g == 0) {
+#pragma unroll
+      for (int j = 0; j < G - 1; ++j) O += s_o[j][d];
+    }
+  }
   const int h = kvh * 4 + hh;
   if (c.world > 0) {  // partial of a split over devices, sent to every rank
     publish_record(c, h, M, L, O);
     return;
   }
+  if (t >= HD) return;
   if (c.record) {  // partial of a split over devices: keep it unnormalised
     float* rec = c.record + h * (HD + 2);
     if (t == 0) { rec[0] = M; rec[1] = L; }
     rec[2 + t] = O;
     return;
   }
-  const float g = bf2f(c.proj[(int64_t)b * 10240 + h * 2 * HD + HD + t]);
-  c.out[(int64_t)b * 4096 + h * HD + t] = f2bf((O / L) * gate_sigmoid(g, c.ref_math));
+  const float gt = bf2f(c.proj[(int64_t)b * 10240 + h * 2 * HD + HD + t]);
+  c.out[(int64_t)b * 4096 + h * HD + t] = f2bf((O / L) * gate_sigmoid(gt, c.ref_math));
 }
 
 // Cross-device merge: one CTA per head, thread = dimension.
@@ -642,6 +659,10 @@ __global__ void __launch_bounds__(256) attn_merge_records_kernel(const float* re
 __global__ void __launch_bounds__(256) attn_merge_mailbox_kernel(const MailboxMergeArgs m) {
   __shared__ int ok;
   const int h = blockIdx.x, t = threadIdx.x;
+  // the next kernel may be scheduled now (its griddepcontrol.wait still waits
+  // for this grid to complete); this grid was scheduled while the record
+  // kernel ran and waits on the counters, not on the stream
+  griddep_launch();
   if (t == 0) ok = 1;
   const uint32_t step = m.done[m.layer] + 1u;
   if (t == 0) {
@@ -697,8 +718,16 @@ __global__ void __launch_bounds__(256) attn_merge_mailbox_kernel(const MailboxMe
 }  // namespace
 
 cudaError_t launch_attn_merge_mailbox(const MailboxMergeArgs& m, cudaStream_t s) {
-  attn_merge_mailbox_kernel<<<16, 256, 0, s>>>(m);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = QC_ATTN_PDL;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(16, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attn_merge_mailbox_kernel, m);
 }
 
 cudaError_t launch_attn_merge_records(const float* records, int32_t n_parts, const uint16_t* proj,
@@ -736,11 +765,16 @@ cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CU
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cc = {};
   cc.gridDim = dim3(c.n * 4, 4, 1);
-  cc.blockDim = dim3(256, 1, 1);
   cc.stream = s;
   cc.attrs = attr;
   cc.numAttrs = 1;
-  return cudaLaunchKernelEx(&cc, attn_combine_kernel, c);
+  // few sequences: many slots per pair, split the merge chain four ways
+  if (c.n <= 2) {
+    cc.blockDim = dim3(1024, 1, 1);
+    return cudaLaunchKernelEx(&cc, attn_combine_kernel<4>, c);
+  }
+  cc.blockDim = dim3(256, 1, 1);
+  return cudaLaunchKernelEx(&cc, attn_combine_kernel<1>, c);
 }
 
 }  // namespace qc
