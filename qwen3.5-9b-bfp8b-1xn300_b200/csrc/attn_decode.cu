@@ -30,6 +30,14 @@
 // K and V into the page (src/engine.cpp:3521-3526); the new token is attended
 // from shared memory, so no CTA reads a row another CTA is writing.
 //
+// Kernel 1b, attn_partial_tc_kernel (the launcher picks it when each CTA
+// streams at most QC_ATTN_TC_MAX_PER page-heads): the same split and records
+// with the products on the fifth-generation tensor cores — tcgen05.mma issued
+// by one thread, accumulators in tensor memory, softmax in four warps that
+// read the scores with tcgen05.ld.  The new token's K / V row is written into
+// the landed tile in shared memory before the MMAs read it, and V rows past a
+// tile's valid length are zeroed (0 * Inf would otherwise reach O).
+//
 // Kernel 2, attn_combine_kernel: per (sequence, kv-head) merges the partial
 // records of the CTAs that covered it, divides by the softmax sum and applies
 // the sigmoid output gate (src/engine.cpp:3560-3563), storing bf16.
@@ -37,6 +45,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace qc {
 namespace {
@@ -184,10 +193,42 @@ __device__ __forceinline__ TileInfo tile_info(const AttnArgs& a, const Cursor& c
   return t;
 }
 
+// tile_info without the page for a cursor whose sequence changes rarely: the
+// sequence's descriptor entries are loaded when it changes, so a loop of
+// single-thread roles over the tiles issues no global loads per tile.
+struct SeqRows {
+  int b = -1, pos = 0, page0 = 0, append = 0;
+  __device__ __forceinline__ TileInfo at(const AttnArgs& a, const Cursor& c) {
+    if (c.b != b) {
+      b = c.b;
+      pos = a.pos[b];
+      page0 = a.page0[b];
+      append = a.append[b];
+    }
+    TileInfo t;
+    const int start = (page0 + c.pg) * PAGE;
+    t.rows_cached = min(max(pos - start, 0), PAGE);
+    t.append_here = (append && pos >= start && pos < start + PAGE) ? 1 : 0;
+    t.page_id = 0;
+    t.tile_len = t.rows_cached + t.append_here;
+    return t;
+  }
+};
+
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+// The tensor-core kernel runs when each CTA streams at most this many
+// page-heads: its one MMA-issuing thread costs ~70 cycles per tcgen05.mma
+// (16 per page-head for the scores), which a short range hides behind its
+// shorter ramp; longer ranges stream faster through the eight mma.sync
+// consumer warps.  Measured crossover (attention time per step, 4096-token
+// contexts): 1 / 4 / 8 sequences 21 / 7 / 5% faster on the tensor-core
+// kernel, 16 even, 32 and 64 2 and 4% slower.
+#ifndef QC_ATTN_TC_MAX_PER
+#define QC_ATTN_TC_MAX_PER 20
+#endif
 #ifndef QC_ATTN_PDL
 #define QC_ATTN_PDL 1
 #endif
@@ -524,6 +565,474 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (cur_b >= 0) flush();
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core (tcgen05) variant of the partial kernel, for short ranges per
+// CTA (QC_ATTN_TC_MAX_PER): the same split, tiles and records, with the dot
+// products issued by one thread into tensor memory (TMEM):
+//   S^T[64 pos x 16] = K[64 x 256] . Qx^T     (M 64, N 16, both K-major)
+//   O[128 x 256]    += Px[128 x 64] . V       (M 128, N 256, V MN-major)
+// Qx and Px have 8 distinct rows (rows 0-3: the bf16 value of the 4 heads'
+// q / p, rows 4-7: the bf16 rounding residual); their descriptors use a zero
+// stride between 8-row groups, so every further group repeats those 8 rows.
+// S^T: position 16w + l sits in TMEM lane 32w + l (l < 16), its 16 columns
+// the scores against the 8 rows twice, so lane l of softmax warp w holds the
+// 4 heads' scores of one position.  O: row r in lane r, repeated in every
+// 32-lane quarter; warp w rescales and stores columns 64w..64w+63 of its own
+// copy.  Warps 5 and 6 stream the K and V rings separately (a K slot frees
+// when its scores are done, a V slot after P . V); the four softmax warps
+// agree on the lazy reference maximum through shared memory once per tile.
+constexpr int TC_THREADS = 7 * 32;            // warps 0-3 softmax, 4 MMA, 5 TMA K, 6 TMA V
+constexpr int TC_MMA = 4, TC_TMA = 5;
+constexpr uint32_t TC_TMEM_COLS = 512;        // S x 2 (64 each) + O (256)
+
+struct __align__(1024) TcSmem {
+  uint16_t k[STAGES][TILE_ELEMS];   // swizzled: [col block 4][row 64][128 B]
+  uint16_t v[STAGES][TILE_ELEMS];
+  uint16_t q[2][4 * 8 * 64];        // per pair parity: [col block 4][row 8][128 B]
+  uint16_t p[2][8 * 64];            // per tile parity: [row 8][128 B]
+  uint16_t knew[2][HD];             // per pair parity: the appended K / V row
+  uint16_t vnew[2][HD];
+  float s_mx[2][4][4];              // per tile parity: [warp][head] max over 16 positions
+  float s_l[4][4];                  // [warp][head] softmax sums at a flush
+  uint64_t full[STAGES], empty[STAGES];      // K ring
+  uint64_t full_v[STAGES], empty_v[STAGES];  // V ring
+  uint64_t s_full[2], s_free[2], p_full[2], o_done[2], q_full[2], fix, xch[2], lx;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ bool tc_need_fix(const TileInfo& t) {
+  return t.tile_len < PAGE || t.append_here;
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    attn_partial_tc_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap tmk,
+                           const __grid_constant__ CUtensorMap tmv) {
+  extern __shared__ unsigned char smem_raw[];
+  TcSmem& sm = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                          ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (!a.early) griddep_wait();
+  const int total = a.split[0], per = a.split[1];
+  const int u_begin = blockIdx.x * per;
+  const int u_end = min(total, u_begin + per);
+  if (u_begin >= u_end) {
+    griddep_wait();  // every thread: the grid completes after its predecessor
+    return;
+  }
+  const int nt = u_end - u_begin;
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+      mbar_init(&sm.full_v[s], 1);
+      mbar_init(&sm.empty_v[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.s_full[b], 1);
+      mbar_init(&sm.s_free[b], 4);
+      mbar_init(&sm.p_full[b], 4);
+      mbar_init(&sm.o_done[b], 1);
+      mbar_init(&sm.q_full[b], 4);
+      mbar_init(&sm.xch[b], 128);
+    }
+    mbar_init(&sm.fix, 4);
+    mbar_init(&sm.lx, 128);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == TC_MMA) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&sm.tmem_base)),
+                 "r"(TC_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const uint32_t t_o = tmem + 128;
+  volatile int* abort_flag = &sm.abort;
+
+  if (warp >= TC_TMA) {
+    // ------------------------------------------------------------ producers
+    // warp 5 streams the K ring, warp 6 the V ring: a K slot is free again as
+    // soon as its scores are computed, a V slot only after P . V
+    const bool is_v = warp == TC_TMA + 1;
+    uint64_t* fbar = is_v ? sm.full_v : sm.full;
+    uint64_t* ebar = is_v ? sm.empty_v : sm.empty;
+    const CUtensorMap* tmap = is_v ? &tmv : &tmk;
+    int i = 0;
+    int last_issued[STAGES];
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) last_issued[s] = -1;
+    bool ok_all = true;
+    for (int base = u_begin; base < u_end && ok_all; base += 32) {
+      const int u = base + lane;
+      int pid = -1, rows = 0, kvh = 0;
+      if (u < u_end) {
+        Cursor c;
+        c.seek(a, u);
+        const TileInfo t = tile_info(a, c, true);
+        pid = t.page_id;
+        rows = t.rows_cached;
+        kvh = c.kvh;
+      }
+      const int cnt = min(32, u_end - base);
+      for (int j = 0; j < cnt; ++j, ++i) {
+        const int pj = __shfl_sync(FULL_MASK, pid, j);
+        const int rj = __shfl_sync(FULL_MASK, rows, j);
+        const int kj = __shfl_sync(FULL_MASK, kvh, j);
+        int ok = 1;
+        if (lane == 0) {
+          const int s = i % STAGES;
+          if (*abort_flag) ok = 0;
+          if (ok && i >= STAGES && !mbar_wait(&ebar[s], ((i / STAGES) - 1) & 1, a.err)) ok = 0;
+          if (ok) {
+            if (pj < 0 && !is_v) record_error(a.err, QC_ERR_BOUNDS);
+            const int nbox = (pj >= 0) ? (rj + BOX_ROWS - 1) / BOX_ROWS : 0;
+            mbar_arrive_expect_tx(&fbar[s], uint32_t(nbox * 4 * BOX_BYTES));
+            const int row0 = (pj * 4 + kj) * PAGE;
+            uint16_t* dst = is_v ? sm.v[s] : sm.k[s];
+            for (int rb = 0; rb < nbox; ++rb)
+#pragma unroll
+              for (int cb = 0; cb < 4; ++cb)
+                tma_load_2d(dst + (cb * PAGE * 128 + rb * BOX_BYTES) / 2, tmap, cb * 64,
+                            row0 + rb * BOX_ROWS, &fbar[s]);
+            last_issued[s] = i;
+          } else {
+            *abort_flag = 1;
+          }
+        }
+        if (!__shfl_sync(FULL_MASK, ok, 0)) {
+          ok_all = false;
+          break;
+        }
+      }
+    }
+    // on abort, wait (bounded) for this CTA's own copies in flight
+    if (lane == 0 && *abort_flag) {
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s)
+        if (last_issued[s] >= 0) mbar_wait(&fbar[s], (last_issued[s] / STAGES) & 1, nullptr);
+    }
+    griddep_wait();
+  } else if (warp == TC_MMA) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      // S = Qx . K^T: M 128, N 64, A and B K-major; O^T += V^T . Px^T: M 128
+      // per half, N 16, A (V [pos][dim]) MN-major, B K-major; bf16 operands,
+      // f32 accumulators
+      const uint32_t id_s = (1u << 4) | (1u << 7) | (1u << 10) | ((16u >> 3) << 17) | ((64u >> 4) << 24);
+      const uint32_t id_o = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((256u >> 3) << 17) |
+                            ((128u >> 4) << 24);
+      Cursor cq;
+      cq.seek(a, u_begin);
+      SeqRows rows_q;
+      int pq = -1, qb = -1, qk = -1, fixcnt = 0;
+      bool firstp[2] = {false, false};
+      int issued_s = -1, issued_o = -1;
+      auto issue_qk = [&](int i) -> bool {
+        const TileInfo t = rows_q.at(a, cq);
+        const bool first = cq.b != qb || cq.kvh != qk;
+        if (first) { ++pq; qb = cq.b; qk = cq.kvh; }
+        const int s = i % STAGES, b = i & 1;
+        if (!mbar_wait(&sm.full[s], (i / STAGES) & 1, a.err)) return false;
+        if (tc_need_fix(t)) {
+          if (!mbar_wait(&sm.fix, fixcnt & 1, a.err)) return false;
+          ++fixcnt;
+        }
+        if (first && !mbar_wait(&sm.q_full[pq & 1], (pq >> 1) & 1, a.err)) return false;
+        if (i >= 2 && !mbar_wait(&sm.s_free[b], ((i >> 1) - 1) & 1, a.err)) return false;
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sm.q[pq & 1]), ka = smem_u32(sm.k[s]);
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma(tmem + b * 16, umma_desc(ka + cb * PAGE * 128 + ks * 32, 16, 1024),
+                 umma_desc(qa + cb * 1024 + ks * 32, 16, 0), id_s, (cb | ks) != 0);
+        umma_commit(&sm.s_full[b]);
+        umma_commit(&sm.empty[s]);  // the K slot
+        issued_s = i;
+        firstp[b] = first;
+        cq.next(a);
+        return true;
+      };
+      bool ok = issue_qk(0);
+      for (int i = 0; i < nt && ok; ++i) {
+        if (*abort_flag) { ok = false; break; }
+        // the next tile's scores run while the softmax works on this one
+        if (i + 1 < nt && !(ok = issue_qk(i + 1))) break;
+        if (!(ok = mbar_wait(&sm.p_full[i & 1], (i >> 1) & 1, a.err))) break;
+        const int s = i % STAGES;
+        if (!(ok = mbar_wait(&sm.full_v[s], (i / STAGES) & 1, a.err))) break;
+        tc_fence_after();
+        const uint32_t va = smem_u32(sm.v[s]), pa = smem_u32(sm.p[i & 1]);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma(t_o, umma_desc(pa + kk * 32, 16, 0), umma_desc(va + kk * 2048, PAGE * 128, 1024), id_o,
+               (!firstp[i & 1] || kk > 0) ? 1u : 0u);
+        umma_commit(&sm.o_done[i & 1]);
+        umma_commit(&sm.empty_v[s]);
+        issued_o = i;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        // wait (bounded) for the products in flight before the memory goes
+        if (issued_s >= 0) mbar_wait(&sm.s_full[issued_s & 1], (issued_s >> 1) & 1, nullptr);
+        if (issued_o >= 0) mbar_wait(&sm.o_done[issued_o & 1], (issued_o >> 1) & 1, nullptr);
+      }
+    }
+  } else {
+    // ------------------------------------------------------- softmax warps
+    griddep_wait();
+    griddep_launch();
+    const int r = lane & 7, hq = r & 3;          // S / O row of this lane, its head
+    const uint32_t lane_off = uint32_t(warp * 32) << 16;
+    Cursor c;
+    c.seek(a, u_begin);
+    // Q rows (value, residual) and the appended K / V row of pair X, into the
+    // buffers of parity X & 1 (src/engine.cpp:3497-3526)
+    auto prep = [&](const Cursor& pc, int x) {
+      const int pos = a.pos[pc.b];
+      const float* cs = a.rope_cos + (int64_t)pos * 32;
+      const float* sn = a.rope_sin + (int64_t)pos * 32;
+      const uint16_t* prow = a.proj + (int64_t)pc.b * 10240;
+      {
+        const int h = pc.kvh * 4 + warp;
+        float xv[8];
+        unpack8(*reinterpret_cast<const uint4*>(prow + h * 2 * HD + lane * 8), xv);
+        norm_rope_lane(xv, a.q_norm, cs, sn, lane);
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          uint16_t h0, l0, h1, l1;
+          split_bf16(xv[2 * e], h0, l0);
+          split_bf16(xv[2 * e + 1], h1, l1);
+          hi[e] = uint32_t(h0) | (uint32_t(h1) << 16);
+          lo[e] = uint32_t(l0) | (uint32_t(l1) << 16);
+        }
+        unsigned char* qs = reinterpret_cast<unsigned char*>(sm.q[x & 1]);
+        const int cb = lane >> 3, ch = lane & 7;
+        *reinterpret_cast<uint4*>(qs + cb * 1024 + warp * 128 + ((ch ^ warp) << 4)) =
+            make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(qs + cb * 1024 + (warp + 4) * 128 + ((ch ^ (warp + 4)) << 4)) =
+            make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
+      const int u_app = a.seg[pc.b] + pc.kvh * pc.np + (pc.np - 1);
+      if (a.append[pc.b] && u_app < u_end && warp < 2) {
+        const int page_abs = a.page0[pc.b] + pc.np - 1;
+        const int pid = a.page_table[(int64_t)a.slots[pc.b] * a.pt_stride + page_abs];
+        const bool in_bounds = pid >= 0 && pid < a.max_pages && pos >= page_abs * PAGE &&
+                               pos < (page_abs + 1) * PAGE;
+        const int64_t row_off =
+            (((int64_t)pid * 4 + pc.kvh) * PAGE + (pos - page_abs * PAGE)) * HD + lane * 8;
+        if (warp == 0) {
+          float xv[8];
+          unpack8(*reinterpret_cast<const uint4*>(prow + 8192 + pc.kvh * HD + lane * 8), xv);
+          norm_rope_lane(xv, a.k_norm, cs, sn, lane);
+          uint4 w;
+          w.x = pack_bf16(xv[0], xv[1]);
+          w.y = pack_bf16(xv[2], xv[3]);
+          w.z = pack_bf16(xv[4], xv[5]);
+          w.w = pack_bf16(xv[6], xv[7]);
+          *reinterpret_cast<uint4*>(&sm.knew[x & 1][lane * 8]) = w;
+          if (in_bounds) *reinterpret_cast<uint4*>(a.k_pool + row_off) = w;
+        } else {
+          const uint4 w = *reinterpret_cast<const uint4*>(prow + 9216 + pc.kvh * HD + lane * 8);
+          *reinterpret_cast<uint4*>(&sm.vnew[x & 1][lane * 8]) = w;
+          if (in_bounds) *reinterpret_cast<uint4*>(a.v_pool + row_off) = w;
+        }
+        if (!in_bounds && lane == 0) record_error(a.err, QC_ERR_BOUNDS);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.q_full[x & 1]);
+    };
+    // the cursor of the pair after the one at `pc` (within this CTA's range)
+    auto next_pair = [&](Cursor pc, int u_pc, int& u_next) -> Cursor {
+      const int left = pc.np - pc.pg;  // units of this pair from pc on
+      u_next = u_pc + left;
+      Cursor n = pc;
+      n.pg = pc.np - 1;
+      n.next(a);
+      return n;
+    };
+    // per head: reference maximum (the same in every lane) and this lane's
+    // share of the softmax sum
+    float m_h[4], l_h[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) { m_h[h] = -INFINITY; l_h[h] = 0.0f; }
+    int cur_b = -1, cur_kvh = -1, px = -1, first_i = 0, lxcnt = 0;
+    bool ok = true;
+    auto flush = [&](int il) {
+      // O complete for the pair's last tile
+      if (!(ok = mbar_wait(&sm.o_done[il & 1], (il >> 1) & 1, a.err))) return;
+      tc_fence_after();
+      const int slot = cur_b * 4 + cur_kvh + blockIdx.x;
+#pragma unroll 1
+      for (int hc = 0; hc < 2; ++hc) {
+        float ov[32];
+        tmem_ld32(t_o + lane_off + 64 * warp + 32 * hc, ov);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ov[j] += __shfl_xor_sync(FULL_MASK, ov[j], 4);  // value + residual rows
+        if (lane < 4) {
+          float* dst = a.part_o + ((int64_t)slot * 4 + lane) * HD + 64 * warp + 32 * hc;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(dst + j) = make_float4(ov[j], ov[j + 1], ov[j + 2], ov[j + 3]);
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float lsum = warp_sum(l_h[h]);
+        if (lane == 0) sm.s_l[warp][h] = lsum;
+      }
+      mbar_arrive(&sm.lx);
+      if (!(ok = mbar_wait(&sm.lx, lxcnt & 1, a.err))) return;
+      ++lxcnt;
+      if (warp == 0 && lane < 4) {
+        a.part_m[slot * 4 + lane] = lane == 0 ? m_h[0] : lane == 1 ? m_h[1] : lane == 2 ? m_h[2] : m_h[3];
+        a.part_l[slot * 4 + lane] =
+            (sm.s_l[0][lane] + sm.s_l[1][lane]) + (sm.s_l[2][lane] + sm.s_l[3][lane]);
+      }
+      tc_fence_before();
+    };
+    SeqRows rows_c;
+    prep(c, 0);
+    for (int i = 0, u = u_begin; i < nt && ok; ++i, ++u, c.next(a)) {
+      if (*abort_flag) { ok = false; break; }
+      const int s = i % STAGES, b = i & 1;
+      const TileInfo t = rows_c.at(a, c);
+      const bool first = c.b != cur_b || c.kvh != cur_kvh;
+      const int pxt = px + (first ? 1 : 0);
+      if (tc_need_fix(t)) {
+        // rows past the tile's valid length hold what an earlier sequence
+        // left in a reused page (possibly not finite): P is zero there, but
+        // 0 * Inf would still reach O, so those V rows are zeroed; the new
+        // token's K / V row goes in at its position.  Then the MMA may read.
+        if (!(ok = mbar_wait(&sm.full[s], (i / STAGES) & 1, a.err))) break;
+        if (!(ok = mbar_wait(&sm.full_v[s], (i / STAGES) & 1, a.err))) break;
+        unsigned char* ks = reinterpret_cast<unsigned char*>(sm.k[s]);
+        unsigned char* vs = reinterpret_cast<unsigned char*>(sm.v[s]);
+        const int zr0 = t.tile_len;
+        for (int k = tid; k < (PAGE - zr0) * 32; k += 128) {
+          const int row = zr0 + k / 32, d = (k % 32) * 8;
+          *reinterpret_cast<uint4*>(vs + swz(row, d)) = make_uint4(0, 0, 0, 0);
+        }
+        if (t.append_here && warp < 2) {
+          const int row = t.rows_cached;
+          const uint16_t* src = warp == 0 ? sm.knew[pxt & 1] : sm.vnew[pxt & 1];
+          *reinterpret_cast<uint4*>((warp == 0 ? ks : vs) + swz(row, lane * 8)) =
+              *reinterpret_cast<const uint4*>(src + lane * 8);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.fix);
+      }
+      if (first) {
+        if (cur_b >= 0) {
+          flush(i - 1);
+          if (!ok) break;
+        }
+        cur_b = c.b;
+        cur_kvh = c.kvh;
+        px = pxt;
+        first_i = i;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) { m_h[h] = -INFINITY; l_h[h] = 0.0f; }
+        // the next pair's operands, one pair ahead of the MMA issuer
+        int u_next;
+        const Cursor nc = next_pair(c, u, u_next);
+        if (u_next < u_end) prep(nc, px + 1);
+      }
+      // ---- S^T of positions 16w..16w+15: lane l < 16 holds position
+      // 16w + l, columns 0-7 its scores against the q value (0-3) and
+      // residual (4-7) rows of the 4 heads
+      if (!(ok = mbar_wait(&sm.s_full[b], (i >> 1) & 1, a.err))) break;
+      tc_fence_after();
+      float sv[16];
+      tmem_ld16(tmem + b * 16 + lane_off, sv);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.s_free[b]);
+      const int jp = 16 * warp + lane;  // position in the tile
+      const bool valid = lane < 16 && jp < t.tile_len;
+      float sc[4], mloc[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        sc[h] = valid ? (sv[h] + sv[4 + h]) * SCALE_LOG2 : -INFINITY;
+        mloc[h] = warp_max(sc[h]);
+      }
+      // ---- lazy reference maximum, agreed by the four warps: it moves only
+      // when a score exceeds it by more than 2^RESCALE_SLACK
+      if (lane == 0) {
+#pragma unroll
+        for (int h = 0; h < 4; ++h) sm.s_mx[b][warp][h] = mloc[h];
+      }
+      mbar_arrive(&sm.xch[b]);
+      if (!(ok = mbar_wait(&sm.xch[b], (i >> 1) & 1, a.err))) break;
+      float cf[4];
+      bool any_up = false;
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float mt = fmaxf(fmaxf(sm.s_mx[b][0][h], sm.s_mx[b][1][h]),
+                               fmaxf(sm.s_mx[b][2][h], sm.s_mx[b][3][h]));
+        cf[h] = 1.0f;
+        if (mt > m_h[h] + RESCALE_SLACK) {
+          cf[h] = (m_h[h] == -INFINITY) ? 0.0f : exp2f(m_h[h] - mt);
+          m_h[h] = mt;
+          any_up = true;
+        }
+        l_h[h] *= cf[h];
+      }
+      // P buffer b was read by P . V of tile i - 2
+      if (i >= 2 && !(ok = mbar_wait(&sm.o_done[b], ((i - 2) >> 1) & 1, a.err))) break;
+      if (any_up && i > first_i) {
+        // O up to tile i - 1, this warp's columns, every row by its head's factor
+        if (!(ok = mbar_wait(&sm.o_done[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err))) break;
+        tc_fence_after();
+        const float cr = hq == 0 ? cf[0] : hq == 1 ? cf[1] : hq == 2 ? cf[2] : cf[3];
+#pragma unroll 1
+        for (int hc = 0; hc < 2; ++hc) {
+          float ov[32];
+          tmem_ld32(t_o + lane_off + 64 * warp + 32 * hc, ov);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ov[j] *= cr;
+          tmem_st32(t_o + lane_off + 64 * warp + 32 * hc, ov);
+        }
+      }
+      // ---- P = 2^(s - m) as bf16 value (rows 0-3) and residual (rows 4-7),
+      // column jp of the [8][64] tile
+      if (lane < 16) {
+        unsigned char* ps = reinterpret_cast<unsigned char*>(sm.p[b]) + (jp & 7) * 2;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float pv = (sc[h] == -INFINITY) ? 0.0f : exp2f(sc[h] - m_h[h]);
+          l_h[h] += pv;
+          uint16_t hi, lo;
+          split_bf16(pv, hi, lo);
+          *reinterpret_cast<uint16_t*>(ps + h * 128 + (((jp >> 3) ^ h) << 4)) = hi;
+          *reinterpret_cast<uint16_t*>(ps + (h + 4) * 128 + (((jp >> 3) ^ (h + 4)) << 4)) = lo;
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.p_full[b]);
+    }
+    if (ok && cur_b >= 0) flush(nt - 1);
+    if (!ok) *abort_flag = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == TC_MMA) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS));
+  }
+}
+
 // Writes head h's record (m, l, o[thread]) into slot [step & 1][layer][rank]
 // of every rank's mailbox over NVLink (plain peer stores), then — once the
 // CTA's stores are visible system-wide — adds 1 to counter [layer][rank] of
@@ -736,7 +1245,9 @@ cudaError_t launch_attn_merge_records(const float* records, int32_t n_parts, con
   return cudaGetLastError();
 }
 
-int attn_smem_bytes() { return static_cast<int>(sizeof(Smem)) + 1024; }
+int attn_smem_bytes() {
+  return static_cast<int>(sizeof(Smem) > sizeof(TcSmem) ? sizeof(Smem) : sizeof(TcSmem)) + 1024;
+}
 
 cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CUtensorMap& tmk,
                                const CUtensorMap& tmv, cudaStream_t s) {
@@ -749,6 +1260,9 @@ cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CU
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          attn_smem_bytes());
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(attn_partial_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             attn_smem_bytes());
+    if (e != cudaSuccess) return e;
     configured.mark(dev);
   }
   cudaLaunchAttribute attr[1];
@@ -756,12 +1270,14 @@ cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CU
   attr[0].val.programmaticStreamSerializationAllowed = QC_ATTN_PDL;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.grid, 1, 1);
-  cfg.blockDim = dim3(THREADS, 1, 1);
+  const bool tc = a.per_hint > 0 && a.per_hint <= QC_ATTN_TC_MAX_PER;
+  cfg.blockDim = dim3(tc ? TC_THREADS : THREADS, 1, 1);
   cfg.dynamicSmemBytes = attn_smem_bytes();
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_partial_kernel, a, tmk, tmv);
+  cudaError_t e =
+      cudaLaunchKernelEx(&cfg, tc ? attn_partial_tc_kernel : attn_partial_kernel, a, tmk, tmv);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cc = {};
   cc.gridDim = dim3(c.n * 4, 4, 1);

@@ -195,6 +195,7 @@ extern "C" int qc_attn_decode_noalloc(const uint16_t* proj_dev, uint16_t* k_pool
   a.part_m = su.scratch + M_OFF;
   a.part_l = su.scratch + L_OFF;
   a.split = desc + 5 * n + 1;
+  a.per_hint = per;
   a.n = n;
   a.grid = su.nsm;
   a.err = reinterpret_cast<int*>(su.scratch + E_OFF);

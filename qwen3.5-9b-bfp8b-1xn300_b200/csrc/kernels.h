@@ -89,6 +89,8 @@ struct AttnArgs {
   int32_t grid;              // CTAs (the SM count; CTAs past the work exit)
   int32_t early;             // 1: no kernel of the open step writes this layer's K/V pool,
                              //    the page table or the descriptor before this launch
+  int32_t per_hint;          // page-heads per CTA as the host last computed them (0: not
+                             //    known); picks the kernel, not the split
   int* err;
 };
 // Combine the partials of each (sequence, kv-head) pair, apply the gate and

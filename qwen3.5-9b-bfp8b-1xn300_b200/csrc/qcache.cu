@@ -105,6 +105,7 @@ struct qc_ctx {
   float* pf_rec = nullptr;      // prefill: records [4][pf_split][128][260] f32
   float* pf_conv = nullptr;     // prefill: conv outputs [32][8192] f32
   int32_t pf_split = 0;
+  int32_t p_per = 0;            // split over devices: page-heads per CTA of the open range
   std::vector<CUtensorMap> tm_k, tm_v;  // per attention layer, for the TMA tile loads
 
   // pinned staging ring for host -> device uploads
@@ -857,6 +858,7 @@ int qc_attn_decode(qc_ctx* c, int layer, const uint16_t* proj, uint16_t* out, qc
   a.part_l = c->part_l;
   a.part_o = c->part_o;
   a.split = c->desc + 5 * n + 1;
+  a.per_hint = c->b_per;
   a.n = n;
   a.grid = c->b_grid;
   a.err = err_site(c, EK_ATTN_DECODE, layer);
@@ -1295,6 +1297,7 @@ int qc_attn_partial_range(qc_ctx* c, int32_t page_begin, int32_t page_end, int32
   if (rc) return rc;
   const int32_t total = 4 * (page_end - page_begin);
   const int32_t per = std::max(1, (total + c->nsm - 1) / c->nsm);
+  c->p_per = per;
   // one-sequence descriptor: slot | pos | seg[2] | page0 | append | total, per
   int32_t d[8] = {s, pos, 0, total, page_begin, append ? 1 : 0, total, per};
   char* buf = nullptr;
@@ -1328,6 +1331,7 @@ int qc_attn_partial(qc_ctx* c, int layer, const uint16_t* proj, float* partial,
   a.page0 = c->desc_part + 4;
   a.append = c->desc_part + 5;
   a.split = c->desc_part + 6;
+  a.per_hint = c->p_per;
   a.q_norm = c->q_norm + layer * HD;
   a.k_norm = c->k_norm + layer * HD;
   a.rope_cos = c->rope_cos;
@@ -1480,6 +1484,7 @@ int qc_attn_partial_p2p(qc_ctx* c, int layer, const uint16_t* proj, qc_stream st
   a.page0 = c->desc_part + 4;
   a.append = c->desc_part + 5;
   a.split = c->desc_part + 6;
+  a.per_hint = c->p_per;
   a.q_norm = c->q_norm + layer * HD;
   a.k_norm = c->k_norm + layer * HD;
   a.rope_cos = c->rope_cos;
