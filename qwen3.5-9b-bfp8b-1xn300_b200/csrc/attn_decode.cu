@@ -745,13 +745,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (first && !mbar_wait(&sm.q_full[pq & 1], (pq >> 1) & 1, a.err)) return false;
         if (i >= 2 && !mbar_wait(&sm.s_free[b], ((i >> 1) - 1) & 1, a.err)) return false;
         tc_fence_after();
-        const uint32_t qa = smem_u32(sm.q[pq & 1]), ka = smem_u32(sm.k[s]);
+        // the start address is the descriptor's low field (address / 16, below
+        // 2^14 for any shared-memory address): steps along the tile are adds
+        const uint64_t dk = umma_desc(smem_u32(sm.k[s]), 16, 1024);
+        const uint64_t dq = umma_desc(smem_u32(sm.q[pq & 1]), 16, 0);
+        const uint32_t ts = tmem + b * 16;
 #pragma unroll
         for (int cb = 0; cb < 4; ++cb)
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
-            umma(tmem + b * 16, umma_desc(ka + cb * PAGE * 128 + ks * 32, 16, 1024),
-                 umma_desc(qa + cb * 1024 + ks * 32, 16, 0), id_s, (cb | ks) != 0);
+            umma(ts, dk + uint64_t((cb * PAGE * 128 + ks * 32) >> 4),
+                 dq + uint64_t((cb * 1024 + ks * 32) >> 4), id_s, (cb | ks) != 0);
         umma_commit(&sm.s_full[b]);
         umma_commit(&sm.empty[s]);  // the K slot
         issued_s = i;
@@ -768,11 +772,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int s = i % STAGES;
         if (!(ok = mbar_wait(&sm.full_v[s], (i / STAGES) & 1, a.err))) break;
         tc_fence_after();
-        const uint32_t va = smem_u32(sm.v[s]), pa = smem_u32(sm.p[i & 1]);
+        const uint64_t dp = umma_desc(smem_u32(sm.p[i & 1]), 16, 0);
+        const uint64_t dv = umma_desc(smem_u32(sm.v[s]), PAGE * 128, 1024);
+        const uint32_t acc0 = firstp[i & 1] ? 0u : 1u;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          umma(t_o, umma_desc(pa + kk * 32, 16, 0), umma_desc(va + kk * 2048, PAGE * 128, 1024), id_o,
-               (!firstp[i & 1] || kk > 0) ? 1u : 0u);
+          umma(t_o, dp + uint64_t((kk * 32) >> 4), dv + uint64_t((kk * 2048) >> 4), id_o,
+               kk > 0 ? 1u : acc0);
         umma_commit(&sm.o_done[i & 1]);
         umma_commit(&sm.empty_v[s]);
         issued_o = i;
@@ -1065,57 +1071,72 @@ __device__ __forceinline__ void publish_record(const CombineArgs& c, int h, floa
 template <int G>
 __global__ void __launch_bounds__(256 * G) attn_combine_kernel(const CombineArgs c) {
   constexpr int NT = 256 * G, NW = NT / 32;
+  constexpr int KO = 8;  // o slots per thread loaded with m and l, before the weights are known
+  static_assert(NT >= 256, "one slot per thread: a pair has at most one slot per CTA, plus one");
   __shared__ float s_w[512];
-  __shared__ float s_red[NW];
+  __shared__ float s_rm[NW], s_rl[NW];
   __shared__ float s_o[G > 1 ? G - 1 : 1][HD];
-  griddep_wait();  // the partial records of the kernel before
-  griddep_launch();
   const int pair = blockIdx.x, hh = blockIdx.y;
   const int b = pair >> 2, kvh = pair & 3, t = threadIdx.x;
-  const int np = (c.seg[b + 1] - c.seg[b]) >> 2;
-  const int u0 = c.seg[b] + kvh * np;
-  const int per = c.split[1];
+  const int h = kvh * 4 + hh;
+  // Loads of what no kernel of the open step writes (the descriptor) or what
+  // was complete when this grid was launched (the projection rows: the
+  // partial kernel triggers its dependents only after its own wait on them)
+  // go before the wait for the partial records.
+  const int seg0 = c.seg[b], seg1 = c.seg[b + 1], per = c.split[1];
+  const bool gated = c.world == 0 && c.record == nullptr;
+  const float gt = (gated && t < HD) ? bf2f(c.proj[(int64_t)b * 10240 + h * 2 * HD + HD + t]) : 0.0f;
+  griddep_wait();  // the partial records of the kernel before
+  griddep_launch();
+  const int np = (seg1 - seg0) >> 2;
+  const int u0 = seg0 + kvh * np;
   if (np == 0) {  // empty page range (split over devices): an empty record
     if (c.world > 0) {
-      publish_record(c, kvh * 4 + hh, -INFINITY, 0.0f, 0.0f);
+      publish_record(c, h, -INFINITY, 0.0f, 0.0f);
       return;
     }
-    float* rec = c.record + (kvh * 4 + hh) * (HD + 2);
+    float* rec = c.record + h * (HD + 2);
     if (t == 0) { rec[0] = -INFINITY; rec[1] = 0.0f; }
     if (t < HD) rec[2 + t] = 0.0f;
     return;
   }
   const int c0 = u0 / per, ns = (u0 + np - 1) / per - c0 + 1;
   const int base = pair + c0;
-  // max over the slots
-  float m = -INFINITY;
-  for (int k = t; k < ns; k += NT) m = fmaxf(m, c.part_m[(base + k) * 4 + hh]);
-  m = warp_max(m);
-  if ((t & 31) == 0) s_red[t >> 5] = m;
-  __syncthreads();
-  float M = s_red[0];
+  const int d = t & (HD - 1), g = t / HD;
+  // every record load at once: m and l of slot t, o of this group's first
+  // KO slots
+  const float mk = t < ns ? c.part_m[(base + t) * 4 + hh] : -INFINITY;
+  const float lk = t < ns ? c.part_l[(base + t) * 4 + hh] : 0.0f;
+  const float* po = c.part_o + ((int64_t)base * 4 + hh) * HD + d;
+  float ov[KO];
 #pragma unroll
-  for (int w = 1; w < NW; ++w) M = fmaxf(M, s_red[w]);
-  __syncthreads();
-  // slot weights and the softmax sum
-  float l = 0.0f;
-  for (int k = t; k < ns; k += NT) {
-    const float mk = c.part_m[(base + k) * 4 + hh];
-    const float f = (mk == -INFINITY) ? 0.0f : exp2f(mk - M);
-    s_w[k] = f;
-    l = fmaf(f, c.part_l[(base + k) * 4 + hh], l);
+  for (int j = 0; j < KO; ++j) {
+    const int k = g + j * G;
+    ov[j] = k < ns ? po[(int64_t)k * 4 * HD] : 0.0f;
   }
-  l = warp_sum(l);
-  if ((t & 31) == 0) s_red[t >> 5] = l;
+  // max over the slots, then the slot weights and the softmax sum
+  const float mw = warp_max(mk);
+  if ((t & 31) == 0) s_rm[t >> 5] = mw;
+  __syncthreads();
+  float M = s_rm[0];
+#pragma unroll
+  for (int w = 1; w < NW; ++w) M = fmaxf(M, s_rm[w]);
+  const float f = (mk == -INFINITY) ? 0.0f : exp2f(mk - M);
+  if (t < ns) s_w[t] = f;
+  const float lw = warp_sum(f * lk);
+  if ((t & 31) == 0) s_rl[t >> 5] = lw;
   __syncthreads();
   float L = 0.0f;
 #pragma unroll
-  for (int w = 0; w < NW; ++w) L += s_red[w];
-  const int d = t & (HD - 1), g = t / HD;
+  for (int w = 0; w < NW; ++w) L += s_rl[w];
   float O = 0.0f;
-  const float* po = c.part_o + ((int64_t)base * 4 + hh) * HD + d;
+#pragma unroll
+  for (int j = 0; j < KO; ++j) {
+    const int k = g + j * G;
+    if (k < ns) O = fmaf(s_w[k], ov[j], O);
+  }
 #pragma unroll 8
-  for (int k = g; k < ns; k += G) O = fmaf(s_w[k], po[(int64_t)k * 4 * HD], O);
+  for (int k = g + KO * G; k < ns; k += G) O = fmaf(s_w[k], po[(int64_t)k * 4 * HD], O);
   if constexpr (G > 1) {
     if (g > 0) s_o[g - 1][d] = O;
     __syncthreads();
@@ -1124,7 +1145,6 @@ __global__ void __launch_bounds__(256 * G) attn_combine_kernel(const CombineArgs
       for (int j = 0; j < G - 1; ++j) O += s_o[j][d];
     }
   }
-  const int h = kvh * 4 + hh;
   if (c.world > 0) {  // partial of a split over devices, sent to every rank
     publish_record(c, h, M, L, O);
     return;
@@ -1136,7 +1156,6 @@ __global__ void __launch_bounds__(256 * G) attn_combine_kernel(const CombineArgs
     rec[2 + t] = O;
     return;
   }
-  const float gt = bf2f(c.proj[(int64_t)b * 10240 + h * 2 * HD + HD + t]);
   c.out[(int64_t)b * 4096 + h * HD + t] = f2bf((O / L) * gate_sigmoid(gt, c.ref_math));
 }
 
