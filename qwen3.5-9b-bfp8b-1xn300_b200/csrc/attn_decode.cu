@@ -1191,6 +1191,9 @@ __global__ void __launch_bounds__(256) attn_merge_mailbox_kernel(const MailboxMe
   // for this grid to complete); this grid was scheduled while the record
   // kernel ran and waits on the counters, not on the stream
   griddep_launch();
+  // the gate half of the projection row was complete before the record
+  // kernel triggered this launch: load it while the records travel
+  const float gt = bf2f(m.proj[h * 2 * HD + HD + t]);
   if (t == 0) ok = 1;
   const uint32_t step = m.done[m.layer] + 1u;
   if (t == 0) {
@@ -1236,7 +1239,6 @@ __global__ void __launch_bounds__(256) attn_merge_mailbox_kernel(const MailboxMe
     L = fmaf(f, __ldcg(r + 1), L);
     O = fmaf(f, __ldcg(r + 2 + t), O);
   }
-  const float gt = bf2f(m.proj[h * 2 * HD + HD + t]);
   m.out[h * HD + t] = f2bf((O / L) * gate_sigmoid(gt, m.ref_math));
   __syncthreads();
   // every CTA read done[layer] at its start; the 16th to get here advances it
