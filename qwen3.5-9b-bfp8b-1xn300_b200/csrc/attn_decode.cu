@@ -220,14 +220,14 @@ __device__ __forceinline__ void griddep_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 // The tensor-core kernel runs when each CTA streams at most this many
-// page-heads: its one MMA-issuing thread costs ~70 cycles per tcgen05.mma
-// (16 per page-head for the scores), which a short range hides behind its
-// shorter ramp; longer ranges stream faster through the eight mma.sync
-// consumer warps.  Measured crossover (attention time per step, 4096-token
-// contexts): 1 / 4 / 8 sequences 21 / 7 / 5% faster on the tensor-core
-// kernel, 16 even, 32 and 64 2 and 4% slower.
+// page-heads: it wins on short ranges (shorter ramp), while on long ones the
+// per-tile chain of its single MMA-issuing thread and four softmax warps
+// lets the eight mma.sync consumer warps stream slightly faster.  Measured
+// (attention time per step, 4096-token contexts): 8 / 16 sequences (15 / 29
+// page-heads per CTA) 8 / 4% faster on the tensor-core kernel, 32 sequences
+// (57) and one 131072-token sequence (56) even, 64 sequences (113) 4% slower.
 #ifndef QC_ATTN_TC_MAX_PER
-#define QC_ATTN_TC_MAX_PER 20
+#define QC_ATTN_TC_MAX_PER 60
 #endif
 #ifndef QC_ATTN_PDL
 #define QC_ATTN_PDL 1
@@ -575,7 +575,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 // q / p, rows 4-7: the bf16 rounding residual); their descriptors use a zero
 // stride between 8-row groups, so every further group repeats those 8 rows.
 // S^T: position 16w + l sits in TMEM lane 32w + l (l < 16), its 16 columns
-// the scores against the 8 rows twice, so lane l of softmax warp w holds the
+// the scores against the 8 rows twice (four accumulators, one per 64-dim
+// block of the head, added after the load), so lane l of softmax warp w holds the
 // 4 heads' scores of one position.  O: row r in lane r, repeated in every
 // 32-lane quarter; warp w rescales and stores columns 64w..64w+63 of its own
 // copy.  Warps 5 and 6 stream the K and V rings separately (a K slot frees
@@ -749,13 +750,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // 2^14 for any shared-memory address): steps along the tile are adds
         const uint64_t dk = umma_desc(smem_u32(sm.k[s]), 16, 1024);
         const uint64_t dq = umma_desc(smem_u32(sm.q[pq & 1]), 16, 0);
-        const uint32_t ts = tmem + b * 16;
+        // four accumulators (one per 64-dim column block, columns 16cb of
+        // the buffer) so that consecutive MMAs do not wait on each other's
+        // accumulator; the softmax warps add them
+        const uint32_t ts = tmem + b * 64;
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb)
+        for (int ks = 0; ks < 4; ++ks)
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            umma(ts, dk + uint64_t((cb * PAGE * 128 + ks * 32) >> 4),
-                 dq + uint64_t((cb * 1024 + ks * 32) >> 4), id_s, (cb | ks) != 0);
+          for (int cb = 0; cb < 4; ++cb)
+            umma(ts + 16 * cb, dk + uint64_t((cb * PAGE * 128 + ks * 32) >> 4),
+                 dq + uint64_t((cb * 1024 + ks * 32) >> 4), id_s, ks != 0);
         umma_commit(&sm.s_full[b]);
         umma_commit(&sm.empty[s]);  // the K slot
         issued_s = i;
@@ -959,7 +963,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (!(ok = mbar_wait(&sm.s_full[b], (i >> 1) & 1, a.err))) break;
       tc_fence_after();
       float sv[16];
-      tmem_ld16(tmem + b * 16 + lane_off, sv);
+      {
+        float s01[32], s23[32];
+        tmem_ld32(tmem + b * 64 + lane_off, s01);
+        tmem_ld32(tmem + b * 64 + lane_off + 32, s23);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sv[j] = (s01[j] + s01[16 + j]) + (s23[j] + s23[16 + j]);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.s_free[b]);
