@@ -338,6 +338,18 @@ int qc_attn_decode_noalloc(const uint16_t* proj_dev, uint16_t* k_pool_dev, uint1
  * code (message in qc_last_error(NULL)) and clears it.  Allocates nothing. */
 int qc_attn_noalloc_check(qc_stream stream);
 
+/* Which decode-attention kernel later launches use (no counterpart in the
+ * reference, whose attention is one host loop): QC_ATTN_KERNEL_AUTO, the
+ * default, takes the tcgen05 kernel when each CTA streams at most 60
+ * page-heads and the mma.sync kernel otherwise; the other two force one.
+ * Both compute the same records (within f32 summation order).  Process-wide,
+ * for tests and tuning; a captured graph keeps the kernel it was captured
+ * with.  Returns the previous mode, or -QC_ERR_ARG for an unknown mode. */
+#define QC_ATTN_KERNEL_AUTO 0
+#define QC_ATTN_KERNEL_MMA  1
+#define QC_ATTN_KERNEL_TC   2
+int qc_attn_select_kernel(int mode);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,6 +41,7 @@
 // Kernel 2, attn_combine_kernel: per (sequence, kv-head) merges the partial
 // records of the CTAs that covered it, divides by the softmax sum and applies
 // the sigmoid output gate (src/engine.cpp:3560-3563), storing bf16.
+#include <atomic>
 #include <cmath>
 
 #include "common.cuh"
@@ -1280,6 +1281,10 @@ int attn_smem_bytes() {
   return static_cast<int>(sizeof(Smem) > sizeof(TcSmem) ? sizeof(Smem) : sizeof(TcSmem)) + 1024;
 }
 
+namespace {
+std::atomic<int> g_attn_mode{QC_ATTN_KERNEL_AUTO};
+}  // namespace
+
 cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CUtensorMap& tmk,
                                const CUtensorMap& tmv, cudaStream_t s) {
   if (a.n <= 0) return cudaSuccess;
@@ -1301,7 +1306,9 @@ cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CU
   attr[0].val.programmaticStreamSerializationAllowed = QC_ATTN_PDL;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.grid, 1, 1);
-  const bool tc = a.per_hint > 0 && a.per_hint <= QC_ATTN_TC_MAX_PER;
+  const int mode = g_attn_mode.load(std::memory_order_relaxed);
+  const bool tc = mode == QC_ATTN_KERNEL_TC ||
+                  (mode == QC_ATTN_KERNEL_AUTO && a.per_hint > 0 && a.per_hint <= QC_ATTN_TC_MAX_PER);
   cfg.blockDim = dim3(tc ? TC_THREADS : THREADS, 1, 1);
   cfg.dynamicSmemBytes = attn_smem_bytes();
   cfg.stream = s;
@@ -1325,3 +1332,9 @@ cudaError_t launch_attn_decode(const AttnArgs& a, const CombineArgs& c, const CU
 }
 
 }  // namespace qc
+
+extern "C" int qc_attn_select_kernel(int mode) {
+  if (mode != QC_ATTN_KERNEL_AUTO && mode != QC_ATTN_KERNEL_MMA && mode != QC_ATTN_KERNEL_TC)
+    return -QC_ERR_ARG;
+  return qc::g_attn_mode.exchange(mode);
+}

@@ -114,6 +114,7 @@ def lib() -> C.CDLL:
         "qc_p2p_reset": (C.c_int, [P, P]),
         "qc_attn_decode_noalloc": (C.c_int, [P, P, P, I32, P, I32, PI32, I32, P, P, P, P, P, P]),
         "qc_attn_noalloc_check": (C.c_int, [P]),
+        "qc_attn_select_kernel": (C.c_int, [C.c_int]),
         "qc_bfp8_packed_bytes": (C.c_int64, [I32, I32]),
         "qc_bfp8_create": (C.c_int, [C.c_int, I32, I32, C.POINTER(P)]),
         "qc_bfp8_destroy": (None, [P]),
@@ -354,6 +355,18 @@ def attn_noalloc_check(stream=0):
     rc = lib().qc_attn_noalloc_check(stream)
     if rc:
         raise QCacheError(rc, lib().qc_last_error(None).decode())
+
+
+ATTN_KERNEL_AUTO, ATTN_KERNEL_MMA, ATTN_KERNEL_TC = 0, 1, 2
+
+
+def attn_select_kernel(mode):
+    """qc_attn_select_kernel: pick the decode-attention kernel process-wide
+    (auto / mma.sync / tcgen05); returns the previous mode."""
+    rc = lib().qc_attn_select_kernel(mode)
+    if rc < 0:
+        raise QCacheError(-rc, f"unknown attention kernel mode {mode}")
+    return rc
 
 
 class Bfp8Matrix:

@@ -21,6 +21,20 @@ def test_library_exports_every_header_symbol(qcache):
         assert hasattr(L, n), n
 
 
+def test_attention_kernel_selection(qcache):
+    """The process-wide kernel choice: auto by default, either kernel forced,
+    unknown modes refused without changing it."""
+    prev = qcache.attn_select_kernel(qcache.ATTN_KERNEL_TC)
+    try:
+        assert prev == qcache.ATTN_KERNEL_AUTO
+        assert qcache.attn_select_kernel(qcache.ATTN_KERNEL_MMA) == qcache.ATTN_KERNEL_TC
+        with pytest.raises(qcache.QCacheError):
+            qcache.attn_select_kernel(7)
+        assert qcache.attn_select_kernel(qcache.ATTN_KERNEL_AUTO) == qcache.ATTN_KERNEL_MMA
+    finally:
+        qcache.attn_select_kernel(qcache.ATTN_KERNEL_AUTO)
+
+
 def test_create_rejects_bad_config(qcache):
     with pytest.raises(qcache.QCacheError):
         qcache.QCache(max_seqs=0, device=qcache.DEVICE_NONE)

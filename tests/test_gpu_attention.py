@@ -5,6 +5,16 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(autouse=True, params=["mma", "tc"])
+def attn_kernel(request, qcache):
+    """Every test here runs on both decode-attention kernels (the launcher
+    would pick by range length; forcing covers both on every case)."""
+    mode = qcache.ATTN_KERNEL_MMA if request.param == "mma" else qcache.ATTN_KERNEL_TC
+    qcache.attn_select_kernel(mode)
+    yield request.param
+    qcache.attn_select_kernel(qcache.ATTN_KERNEL_AUTO)
+
 torch = pytest.importorskip("torch")
 
 from gpu_util import (assert_out_close, dev, empty_u16, host_u16,  # noqa: E402
