@@ -601,6 +601,7 @@ struct __align__(1024) TcSmem {
   uint64_t s_full[2], s_free[2], p_full[2], o_done[2], q_full[2], fix, xch[2], lx;
   uint32_t tmem_base;
   int abort;
+  int k_seen;                       // K tiles the MMA thread has seen land (monotonic)
 };
 
 __device__ __forceinline__ bool tc_need_fix(const TileInfo& t) {
@@ -641,6 +642,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     mbar_init(&sm.fix, 4);
     mbar_init(&sm.lx, 128);
     sm.abort = 0;
+    sm.k_seen = 0;
     fence_mbar_init();
   }
   if (warp == TC_MMA) {
@@ -689,6 +691,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (lane == 0) {
           const int s = i % STAGES;
           if (*abort_flag) ok = 0;
+          if (ok && is_v && i < STAGES) {
+            // ramp: the first V tiles go out only once their K tile has
+            // landed, so the first scores do not share the HBM burst with them
+            const uint64_t t0 = globaltimer();
+            while (*reinterpret_cast<volatile int*>(&sm.k_seen) <= i && !*abort_flag)
+              if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+                record_error(a.err, QC_ERR_TIMEOUT);
+                ok = 0;
+                break;
+              }
+          }
           if (ok && i >= STAGES && !mbar_wait(&ebar[s], ((i / STAGES) - 1) & 1, a.err)) ok = 0;
           if (ok) {
             if (pj < 0 && !is_v) record_error(a.err, QC_ERR_BOUNDS);
@@ -740,6 +753,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (first) { ++pq; qb = cq.b; qk = cq.kvh; }
         const int s = i % STAGES, b = i & 1;
         if (!mbar_wait(&sm.full[s], (i / STAGES) & 1, a.err)) return false;
+        *reinterpret_cast<volatile int*>(&sm.k_seen) = i + 1;
         if (tc_need_fix(t)) {
           if (!mbar_wait(&sm.fix, fixcnt & 1, a.err)) return false;
           ++fixcnt;
