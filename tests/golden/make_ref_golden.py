@@ -7,8 +7,8 @@ reference: tests/test_ref_pin.py checks the oracle against them on every
 machine, whether or not the reference source is present there.  Inputs are
 not stored; they regenerate from the seeds with the package's synth module.
 
-Needs the reference source (default /root/reference/src, or
-QC_REFERENCE_SRC) and an AVX-512 host.  Run from the repository root:
+Needs the reference source (the directory QC_REFERENCE_SRC names, default as
+in oracle/ref.py) and an AVX-512 host.  Run from the repository root:
     python tests/golden/make_ref_golden.py
 """
 import os
